@@ -1,0 +1,32 @@
+// Host-side launch interface shared by the translation units of libtrcuda.so (not part of the C ABI).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace trc {
+
+struct GemmArgs;
+struct AttnArgs;
+
+// dsp.cu
+void launch_stft(const float* audio, int B, int64_t L, int T, int n, int hop, const float* window, const float2* tw,
+                 float* xin, cudaStream_t st);
+void launch_istft(const float* xin, const float* mask, int B, int T, int n, int hop, const float* window,
+                  const float2* tw_inv, float* frames, float* out, cudaStream_t st);
+void launch_band_split(const float* xin, int width, int rows, int nbands, const int* band_off, const float* wt,
+                       const float* bias, float* X, cudaStream_t st);
+void launch_rownorm(const float* X, void* xn, int64_t rows, float eps, int precision, cudaStream_t st);
+void launch_add_rmsnorm(float* X, const float* Y, void* out, int out_f32, int64_t rows, float eps, int precision,
+                        cudaStream_t st);
+void launch_chunk_ola(const float* chunks, int64_t clen, const int64_t* d_starts, int n_chunks, const float* w,
+                      int64_t n, float* out, cudaStream_t st);
+
+// tc.cu (tensor-core kernels). epi: EpiKind; precision: 0 fp16, 1 bf16. Return cudaError_t of the launch.
+cudaError_t launch_gemm(int epi, int precision, const CUtensorMap& map_a, const CUtensorMap& map_b,
+                        const GemmArgs& args, int num_sms, cudaStream_t st);
+cudaError_t launch_attention(int precision, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
+                             const AttnArgs& args, cudaStream_t st);
+
+}  // namespace trc

@@ -1,0 +1,65 @@
+// Instantiation and launch of the tensor-core kernels (tcgen05 GEMM with fused epilogues, attention).
+#include "attention.cuh"
+#include "gemm.cuh"
+#include "internal.h"
+
+namespace trc {
+
+namespace {
+
+constexpr int kBN = 256;
+constexpr int kStages = 4;
+
+template <int EPI, typename T>
+cudaError_t launch_gemm_t(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& args, int num_sms,
+                          cudaStream_t st) {
+  using S = GemmSmem<kBN, kStages>;
+  auto kern = gemm_kernel<kBN, kStages, EPI, T>;
+  // the attribute is per function and per device: set it on every launch (a cheap host call)
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBytes);
+  if (e != cudaSuccess) return e;
+  if (args.num_tiles <= 0) return cudaSuccess;
+  const int grid = args.num_tiles < num_sms ? args.num_tiles : num_sms;
+  kern<<<grid, kGemmThreads, S::kBytes, st>>>(ma, mb, args);
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t launch_gemm_p(int epi, const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& args, int num_sms,
+                          cudaStream_t st) {
+  switch (epi) {
+    case EPI_QKV: return launch_gemm_t<EPI_QKV, T>(ma, mb, args, num_sms, st);
+    case EPI_RESNORM: return launch_gemm_t<EPI_RESNORM, T>(ma, mb, args, num_sms, st);
+    case EPI_GELU: return launch_gemm_t<EPI_GELU, T>(ma, mb, args, num_sms, st);
+    case EPI_MASK_TANH: return launch_gemm_t<EPI_MASK_TANH, T>(ma, mb, args, num_sms, st);
+    case EPI_MASK_GLU: return launch_gemm_t<EPI_MASK_GLU, T>(ma, mb, args, num_sms, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+template <typename T>
+cudaError_t launch_attention_t(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
+                               const AttnArgs& args, cudaStream_t st) {
+  auto kern = attention_kernel<T>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnSmem::kBytes);
+  if (e != cudaSuccess) return e;
+  if (args.num_tiles <= 0) return cudaSuccess;
+  kern<<<args.num_tiles, kAttnThreads, AttnSmem::kBytes, st>>>(mq, mk, mv, args);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_gemm(int epi, int precision, const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& args,
+                        int num_sms, cudaStream_t st) {
+  return precision == 0 ? launch_gemm_p<__half>(epi, ma, mb, args, num_sms, st)
+                        : launch_gemm_p<__nv_bfloat16>(epi, ma, mb, args, num_sms, st);
+}
+
+cudaError_t launch_attention(int precision, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
+                             const AttnArgs& args, cudaStream_t st) {
+  return precision == 0 ? launch_attention_t<__half>(mq, mk, mv, args, st)
+                        : launch_attention_t<__nv_bfloat16>(mq, mk, mv, args, st);
+}
+
+}  // namespace trc
