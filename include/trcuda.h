@@ -88,6 +88,18 @@ int trc_ola(const float* d_chunks, int64_t chunk_out_len, const int64_t* h_start
 
 const char* trc_last_error(void);
 
+/* ------------------------------------------------------------------ instrumentation
+ * Per-section device timing, the counterpart of the reference's opt-in per-section profile
+ * (FastBSRoformer.timer, turbo_roformer/fast.py:62-80; same section keys: stft, band_split, norm,
+ * qkv_rope_gemm, attention_t, attention_f, gemm_out_res_norm, gemm_ff1, gemm_ff2_res_norm, mask,
+ * istft). trc_profile(h, 1) synchronises the device, clears the totals and records a CUDA event pair
+ * around every section on its launch stream; trc_profile_read writes one "name total_ms launches"
+ * line per section into buf (waiting for the recorded events). trc_launch_count returns the number
+ * of kernels this library has launched in the process. */
+int trc_profile(trc_handle* h, int enable);
+int trc_profile_read(trc_handle* h, char* buf, int buflen);
+long long trc_launch_count(void);
+
 /* ------------------------------------------------------------------ per-stage entry points
  * The op-level surface of the reference (TORCH_LIBRARY(turbo_roformer), kernels.cpp:644-652), on the
  * layouts of this backend. `layer` indexes the 2*depth transformers in forward order (even = time,

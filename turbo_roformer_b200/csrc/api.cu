@@ -5,6 +5,7 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -180,9 +181,58 @@ struct trc_handle {
   DevBuf<float> xin, X, mask, frames;
   DevBuf<uint16_t> xn, Q, K, V, O, H;
   DevBuf<float> G;
+  // section timing (CUDA events on the launch stream, like the reference's per-section _Timer)
+  bool timing = false;
+  std::vector<cudaEvent_t> ev_pool;
+  std::vector<std::pair<std::string, std::pair<cudaEvent_t, cudaEvent_t>>> ev_pending;
+  std::map<std::string, std::pair<double, long>> section;  // name -> (ms, launches)
+  ~trc_handle() {
+    for (auto& e : ev_pool) cudaEventDestroy(e);
+    for (auto& p : ev_pending) {
+      cudaEventDestroy(p.second.first);
+      cudaEventDestroy(p.second.second);
+    }
+  }
 };
 
 namespace {
+
+std::atomic<long long> g_launches{0};
+
+cudaEvent_t pool_event(trc_handle* h) {
+  if (!h->ev_pool.empty()) {
+    cudaEvent_t e = h->ev_pool.back();
+    h->ev_pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  cudaEventCreate(&e);
+  return e;
+}
+
+// Times one stage on `st` when the handle's timing is on; counts the kernel launches it makes.
+struct Section {
+  trc_handle* h;
+  const char* name;
+  cudaStream_t st;
+  int launches;
+  cudaEvent_t e0 = nullptr;
+  Section(trc_handle* h_, const char* n, cudaStream_t s_, int l = 1) : h(h_), name(n), st(s_), launches(l) {
+    if (h->timing) {
+      e0 = pool_event(h);
+      cudaEventRecord(e0, st);
+    }
+  }
+  ~Section() {
+    g_launches += launches;
+    if (h->timing && e0) {
+      cudaEvent_t e1 = pool_event(h);
+      cudaEventRecord(e1, st);
+      h->ev_pending.push_back({name, {e0, e1}});
+      h->section[name].second += launches;
+    }
+  }
+};
 
 const std::vector<float>* param(trc_handle* h, const std::string& name, size_t numel) {
   auto it = h->params.find(name);
@@ -674,22 +724,92 @@ int trc_forward(trc_handle* h, const float* d_audio, int batch, int64_t samples,
   int rc;
   if ((rc = ensure_workspace(h, batch, T))) return rc;
   const int64_t rows = (int64_t)batch * T * h->nb;
-  trc::launch_stft(d_audio, batch, samples, T, h->n_fft, h->hop, h->window.p, h->tw_fwd.p, h->xin.p, st);
-  trc::launch_band_split(h->xin.p, h->width, batch * T, h->nb, h->bs_off.p, h->bs_wt.p, h->bs_bias.p, h->X.p, st);
-  trc::launch_rownorm(h->X.p, h->xn.p, rows, 1e-12f, h->prec, st);
+  {
+    Section sec(h, "stft", st);
+    trc::launch_stft(d_audio, batch, samples, T, h->n_fft, h->hop, h->window.p, h->tw_fwd.p, h->xin.p, st);
+  }
+  {
+    Section sec(h, "band_split", st);
+    trc::launch_band_split(h->xin.p, h->width, batch * T, h->nb, h->bs_off.p, h->bs_wt.p, h->bs_bias.p, h->X.p, st);
+  }
+  {
+    Section sec(h, "norm", st);
+    trc::launch_rownorm(h->X.p, h->xn.p, rows, 1e-12f, h->prec, st);
+  }
   if ((rc = check_launch(cudaGetLastError(), "stft/band split"))) return rc;
   for (int l = 0; l < 2 * h->depth; ++l) {
     const int mode = l & 1;
-    if ((rc = run_qkv(h, l, h->xn.p, batch, T, h->Q.p, h->K.p, h->V.p, h->G.p, st))) return rc;
-    if ((rc = run_attention(h, mode, h->Q.p, h->K.p, h->V.p, h->G.p, h->O.p, batch, T, st))) return rc;
-    if ((rc = run_res_norm(h, l, 0, h->O.p, h->X.p, h->xn.p, rows, st))) return rc;
-    if ((rc = run_gelu(h, l, h->xn.p, h->H.p, rows, st))) return rc;
-    if ((rc = run_res_norm(h, l, 1, h->H.p, h->X.p, h->xn.p, rows, st))) return rc;
+    {
+      Section sec(h, "qkv_rope_gemm", st);
+      if ((rc = run_qkv(h, l, h->xn.p, batch, T, h->Q.p, h->K.p, h->V.p, h->G.p, st))) return rc;
+    }
+    {
+      Section sec(h, mode == 0 ? "attention_t" : "attention_f", st);
+      if ((rc = run_attention(h, mode, h->Q.p, h->K.p, h->V.p, h->G.p, h->O.p, batch, T, st))) return rc;
+    }
+    {
+      Section sec(h, "gemm_out_res_norm", st);
+      if ((rc = run_res_norm(h, l, 0, h->O.p, h->X.p, h->xn.p, rows, st))) return rc;
+    }
+    {
+      Section sec(h, "gemm_ff1", st);
+      if ((rc = run_gelu(h, l, h->xn.p, h->H.p, rows, st))) return rc;
+    }
+    {
+      Section sec(h, "gemm_ff2_res_norm", st);
+      if ((rc = run_res_norm(h, l, 1, h->H.p, h->X.p, h->xn.p, rows, st))) return rc;
+    }
   }
-  if ((rc = run_mask(h, h->xn.p, batch, T, h->mask.p, h->H.p, st))) return rc;
-  trc::launch_istft(h->xin.p, h->mask.p, batch, T, h->n_fft, h->hop, h->window.p, h->tw_inv.p, h->frames.p, d_out, st);
+  {
+    Section sec(h, "mask", st, 2);
+    if ((rc = run_mask(h, h->xn.p, batch, T, h->mask.p, h->H.p, st))) return rc;
+  }
+  {
+    Section sec(h, "istft", st, 2);
+    trc::launch_istft(h->xin.p, h->mask.p, batch, T, h->n_fft, h->hop, h->window.p, h->tw_inv.p, h->frames.p, d_out,
+                      st);
+  }
   return check_launch(cudaGetLastError(), "istft");
 }
+
+int trc_profile(trc_handle* h, int enable) {
+  if (!h) return fail(TRC_E_INVALID, "null handle");
+  TRC_CUDA(cudaSetDevice(h->device));
+  TRC_CUDA(cudaDeviceSynchronize());
+  for (auto& p : h->ev_pending) {
+    h->ev_pool.push_back(p.second.first);
+    h->ev_pool.push_back(p.second.second);
+  }
+  h->ev_pending.clear();
+  h->section.clear();
+  h->timing = enable != 0;
+  return TRC_OK;
+}
+
+int trc_profile_read(trc_handle* h, char* buf, int buflen) {
+  if (!h || !buf || buflen < 1) return fail(TRC_E_INVALID, "bad profile_read arguments");
+  TRC_CUDA(cudaSetDevice(h->device));
+  for (auto& p : h->ev_pending) {
+    TRC_CUDA(cudaEventSynchronize(p.second.second));
+    float ms = 0.f;
+    TRC_CUDA(cudaEventElapsedTime(&ms, p.second.first, p.second.second));
+    h->section[p.first].first += ms;
+    h->ev_pool.push_back(p.second.first);
+    h->ev_pool.push_back(p.second.second);
+  }
+  h->ev_pending.clear();
+  std::string out;
+  char line[160];
+  for (auto& kv : h->section) {
+    snprintf(line, sizeof(line), "%s %.6f %ld\n", kv.first.c_str(), kv.second.first, kv.second.second);
+    out += line;
+  }
+  if ((int)out.size() + 1 > buflen) return fail(TRC_E_INVALID, "profile buffer too small (%zu bytes needed)", out.size() + 1);
+  std::memcpy(buf, out.c_str(), out.size() + 1);
+  return TRC_OK;
+}
+
+long long trc_launch_count(void) { return g_launches.load(); }
 
 int trc_ola(const float* d_chunks, int64_t chunk_out_len, const int64_t* h_starts, int n_chunks, int64_t chunk,
             int64_t n, float* d_result, void* stream) {
@@ -715,6 +835,7 @@ int trc_ola(const float* d_chunks, int64_t chunk_out_len, const int64_t* h_start
   TRC_CUDA(cudaMemcpyAsync(d_w, w.data(), sizeof(float) * chunk, cudaMemcpyHostToDevice, st));
   TRC_CUDA(cudaMemcpyAsync(d_s, h_starts, sizeof(int64_t) * n_chunks, cudaMemcpyHostToDevice, st));
   trc::launch_chunk_ola(d_chunks, chunk_out_len, d_s, n_chunks, d_w, n, d_result, st);
+  g_launches += 1;
   cudaError_t e = cudaGetLastError();
   // pageable-source copies above are staged before returning, so the host vector may go out of scope
   TRC_CUDA(cudaFreeAsync(d_w, st));
@@ -727,6 +848,7 @@ int trc_add_rmsnorm(trc_handle* h, float* d_X, const float* d_Y, void* d_out, in
                     void* stream) {
   TRC_REQUIRE_PREPARED(h);
   if (!d_X || !d_out || rows < 0) return fail(TRC_E_INVALID, "bad add_rmsnorm arguments");
+  Section sec(h, "norm", (cudaStream_t)stream);
   trc::launch_add_rmsnorm(d_X, d_Y, d_out, out_f32, rows, eps, h->prec, (cudaStream_t)stream);
   return check_launch(cudaGetLastError(), "add_rmsnorm");
 }
@@ -735,6 +857,7 @@ int trc_qkv_rope_gemm(trc_handle* h, int layer, const void* d_xn, int batch, int
                       float* d_G, void* stream) {
   TRC_REQUIRE_PREPARED(h);
   if (layer < 0 || layer >= 2 * h->depth || batch < 1 || T < 1) return fail(TRC_E_INVALID, "bad qkv arguments");
+  Section sec(h, "qkv_rope_gemm", (cudaStream_t)stream);
   return run_qkv(h, layer, d_xn, batch, T, d_Q, d_K, d_V, d_G, (cudaStream_t)stream);
 }
 
@@ -742,6 +865,7 @@ int trc_attention(trc_handle* h, int mode, const void* d_Q, const void* d_K, con
                   void* d_O, int batch, int T, void* stream) {
   TRC_REQUIRE_PREPARED(h);
   if ((mode != 0 && mode != 1) || batch < 1 || T < 1) return fail(TRC_E_INVALID, "bad attention arguments");
+  Section sec(h, mode == 0 ? "attention_t" : "attention_f", (cudaStream_t)stream);
   return run_attention(h, mode, d_Q, d_K, d_V, d_G, d_O, batch, T, (cudaStream_t)stream);
 }
 
@@ -750,12 +874,14 @@ int trc_gemm_res_norm(trc_handle* h, int layer, int which, const void* d_A, floa
   TRC_REQUIRE_PREPARED(h);
   if (layer < 0 || layer >= 2 * h->depth || (which != 0 && which != 1) || rows < 1)
     return fail(TRC_E_INVALID, "bad gemm_res_norm arguments");
+  Section sec(h, which == 0 ? "gemm_out_res_norm" : "gemm_ff2_res_norm", (cudaStream_t)stream);
   return run_res_norm(h, layer, which, d_A, d_X, d_xn, rows, (cudaStream_t)stream);
 }
 
 int trc_gemm_gelu(trc_handle* h, int layer, const void* d_xn, void* d_H, int64_t rows, void* stream) {
   TRC_REQUIRE_PREPARED(h);
   if (layer < 0 || layer >= 2 * h->depth || rows < 1) return fail(TRC_E_INVALID, "bad gemm_gelu arguments");
+  Section sec(h, "gemm_ff1", (cudaStream_t)stream);
   return run_gelu(h, layer, d_xn, d_H, rows, (cudaStream_t)stream);
 }
 
@@ -763,6 +889,7 @@ int trc_stft(trc_handle* h, const float* d_audio, int batch, int64_t samples, fl
   TRC_REQUIRE_PREPARED(h);
   if (batch < 1 || samples <= h->n_fft / 2) return fail(TRC_E_INVALID, "bad stft arguments");
   const int T = frames_for(h, samples);
+  Section sec(h, "stft", (cudaStream_t)stream);
   trc::launch_stft(d_audio, batch, samples, T, h->n_fft, h->hop, h->window.p, h->tw_fwd.p, d_xin, (cudaStream_t)stream);
   return check_launch(cudaGetLastError(), "stft");
 }
@@ -770,6 +897,7 @@ int trc_stft(trc_handle* h, const float* d_audio, int batch, int64_t samples, fl
 int trc_band_split(trc_handle* h, const float* d_xin, int batch, int T, float* d_X, void* stream) {
   TRC_REQUIRE_PREPARED(h);
   if (batch < 1 || T < 1) return fail(TRC_E_INVALID, "bad band_split arguments");
+  Section sec(h, "band_split", (cudaStream_t)stream);
   trc::launch_band_split(d_xin, h->width, batch * T, h->nb, h->bs_off.p, h->bs_wt.p, h->bs_bias.p, d_X,
                          (cudaStream_t)stream);
   return check_launch(cudaGetLastError(), "band_split");
@@ -778,6 +906,7 @@ int trc_band_split(trc_handle* h, const float* d_xin, int batch, int T, float* d
 int trc_mask(trc_handle* h, const void* d_xn, int batch, int T, float* d_mask, void* d_hidden, void* stream) {
   TRC_REQUIRE_PREPARED(h);
   if (batch < 1 || T < 1 || !d_hidden) return fail(TRC_E_INVALID, "bad mask arguments");
+  Section sec(h, "mask", (cudaStream_t)stream, 2);
   return run_mask(h, d_xn, batch, T, d_mask, d_hidden, (cudaStream_t)stream);
 }
 
@@ -785,6 +914,7 @@ int trc_istft(trc_handle* h, const float* d_xin, const float* d_mask, int batch,
               void* stream) {
   TRC_REQUIRE_PREPARED(h);
   if (batch < 1 || T < 2 || !d_frames) return fail(TRC_E_INVALID, "bad istft arguments");
+  Section sec(h, "istft", (cudaStream_t)stream, 2);
   trc::launch_istft(d_xin, d_mask, batch, T, h->n_fft, h->hop, h->window.p, h->tw_inv.p, d_frames, d_out,
                     (cudaStream_t)stream);
   return check_launch(cudaGetLastError(), "istft");

@@ -136,12 +136,12 @@ __global__ void __launch_bounds__(256) band_split_kernel(const float* __restrict
                                                          int nbands, const int* __restrict__ band_off,
                                                          const float* __restrict__ wt, const float* __restrict__ bias,
                                                          float* __restrict__ X) {
-  __shared__ float xs[64][65];
+  __shared__ __align__(16) float xs[64][68];  // row stride 68 keeps float4 reads 16-byte aligned
   __shared__ float ssq_s[64];
   const int band = blockIdx.y;
   const int r0 = blockIdx.x * 64;
   const int off = band_off[band];
-  const int din = band_off[band + 1] - off;
+  const int din = band_off[band + 1] - off;  // 4 * bins: always a multiple of 4
   const int o = threadIdx.x;
   float acc[64];
 #pragma unroll
@@ -161,10 +161,14 @@ __global__ void __launch_bounds__(256) band_split_kernel(const float* __restrict
     if (o < 64) {
       for (int col = 0; col < cw; ++col) ssq += xs[o][col] * xs[o][col];
     }
-    for (int i = 0; i < cw; ++i) {
-      const float w = wt[(size_t)(off + c0 + i) * 256 + o];
+    for (int i = 0; i < cw; i += 4) {
+      const float* wp = wt + (size_t)(off + c0 + i) * 256 + o;
+      const float w0 = wp[0], w1 = wp[256], w2 = wp[512], w3 = wp[768];
 #pragma unroll
-      for (int r = 0; r < 64; ++r) acc[r] = fmaf(xs[r][i], w, acc[r]);
+      for (int r = 0; r < 64; ++r) {
+        const float4 xv = *reinterpret_cast<const float4*>(&xs[r][i]);
+        acc[r] = fmaf(xv.w, w3, fmaf(xv.z, w2, fmaf(xv.y, w1, fmaf(xv.x, w0, acc[r]))));
+      }
     }
     __syncthreads();
   }

@@ -157,45 +157,66 @@ __device__ __forceinline__ void epi_qkv(const GemmArgs& a, const TileCoord& tc, 
   }
 }
 
+// Residual add + row L2 norm, warp-cooperative: the warp's 32 rows x 256 columns are moved through a
+// padded shared-memory transpose 32 columns at a time, so X and xn are read and written as coalesced
+// 128-byte row segments (one row per instruction, all 32 rows' loads in flight before any store).
+// Per-lane partial sums of squares (one per row) are combined with a 31-shuffle transpose-reduce that
+// leaves the total of row `lane` in lane `lane`.
 template <int BN, typename TIn>
-__device__ __forceinline__ void epi_resnorm(const GemmArgs& a, const TileCoord& tc, uint32_t taddr, int m,
-                                            bool valid) {
-  float* X = static_cast<float*>(a.out0) + (size_t)m * 256;
-  TIn* xn = static_cast<TIn*>(a.out1) + (size_t)m * 256;
-  float ss = 0.f;
+__device__ __forceinline__ void epi_resnorm(const GemmArgs& a, uint32_t taddr, int row0, int lane,
+                                            float* stage) {
+  float* X = static_cast<float*>(a.out0);
+  TIn* xn = static_cast<TIn*>(a.out1);
+  const int nrows = min(32, a.M - row0);  // rows of this warp that exist (may be <= 0)
+  float ps[32];
+#pragma unroll
+  for (int r = 0; r < 32; ++r) ps[r] = 0.f;
 #pragma unroll 1
   for (int c = 0; c < 8; ++c) {
     float v[32];
     tmem_ld32(taddr + c * 32, v);
-    if (valid) {
-      float4* xp = reinterpret_cast<float4*>(X + c * 32);
-      const float4* bp = a.bias ? reinterpret_cast<const float4*>(a.bias + c * 32) : nullptr;
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        float4 x = xp[q];
-        float4 y = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-        if (bp) {
-          const float4 bb = bp[q];
-          y.x += bb.x; y.y += bb.y; y.z += bb.z; y.w += bb.w;
-        }
-        x.x += y.x; x.y += y.y; x.z += y.z; x.w += y.w;
-        xp[q] = x;
-        ss += x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w;
-      }
+    for (int i = 0; i < 32; ++i) stage[lane * 33 + i] = v[i];
+    __syncwarp();
+    const int col = c * 32 + lane;
+    const float b = a.bias ? a.bias[col] : 0.f;
+    float x[32];
+#pragma unroll
+    for (int r = 0; r < 32; ++r) x[r] = r < nrows ? X[(size_t)(row0 + r) * 256 + col] : 0.f;
+#pragma unroll
+    for (int r = 0; r < 32; ++r) {
+      x[r] += stage[r * 33 + lane] + b;
+      ps[r] = fmaf(x[r], x[r], ps[r]);
+    }
+#pragma unroll
+    for (int r = 0; r < 32; ++r)
+      if (r < nrows) X[(size_t)(row0 + r) * 256 + col] = x[r];
+    __syncwarp();
+  }
+  // transpose-reduce: after the step with offset o, ps[i] (i < o) holds the pair-sum of the row
+  // selected by the lane bits above o
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    const bool upper = (lane & o) != 0;
+#pragma unroll
+    for (int i = 0; i < o; ++i) {
+      const float send = upper ? ps[i] : ps[i + o];
+      const float keep = upper ? ps[i + o] : ps[i];
+      ps[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
     }
   }
-  if (!valid) return;
-  const float inv = 1.0f / fmaxf(sqrtf(ss), a.eps);
+  const float inv = 1.0f / fmaxf(sqrtf(ps[0]), a.eps);  // for row `lane`
 #pragma unroll 1
   for (int c = 0; c < 8; ++c) {
-    const float4* xp = reinterpret_cast<const float4*>(X + c * 32);
-    float v[32];
+    const int col = c * 32 + lane;
+    float x[32];
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      const float4 x = xp[q];
-      v[4 * q] = x.x * inv; v[4 * q + 1] = x.y * inv; v[4 * q + 2] = x.z * inv; v[4 * q + 3] = x.w * inv;
+    for (int r = 0; r < 32; ++r) x[r] = r < nrows ? X[(size_t)(row0 + r) * 256 + col] : 0.f;
+#pragma unroll
+    for (int r = 0; r < 32; ++r) {
+      const float iv = __shfl_sync(0xffffffffu, inv, r);
+      if (r < nrows) xn[(size_t)(row0 + r) * 256 + col] = OperandType<TIn>::from_float(x[r] * iv);
     }
-    store32<TIn>(xn + c * 32, v);
   }
 }
 
@@ -261,7 +282,9 @@ struct GemmSmem {
   static constexpr int kABytes = kGemmBM * kGemmBK * 2;  // 16 KB
   static constexpr int kBBytes = BN * kGemmBK * 2;       // 32 KB at BN = 256
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kBarOffset = STAGES * kStageBytes;
+  static constexpr int kStageOffset = STAGES * kStageBytes;        // epilogue transpose buffers
+  static constexpr int kEpiStageBytes = 4 * 32 * 33 * 4;           // 4 warps x [32][33] fp32
+  static constexpr int kBarOffset = kStageOffset + kEpiStageBytes;
   static constexpr int kBytes = kBarOffset + 256 + 1024;  // + barriers + alignment slack
 };
 
@@ -413,7 +436,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if constexpr (EPI == EPI_QKV) {
         epi_qkv<BN, TIn>(args, tc, taddr, m, valid);
       } else if constexpr (EPI == EPI_RESNORM) {
-        epi_resnorm<BN, TIn>(args, tc, taddr, m, valid);
+        float* stage = reinterpret_cast<float*>(smem + S::kStageOffset) + quarter * 32 * 33;
+        epi_resnorm<BN, TIn>(args, tmem_base + (uint32_t)(buf * BN) + ((uint32_t)(quarter * 32) << 16),
+                             tc.m0 + quarter * 32, lane, stage);
       } else if constexpr (EPI == EPI_GELU) {
         epi_act<BN, TIn>(args, tc, taddr, m, valid, false);
       } else if constexpr (EPI == EPI_MASK_TANH) {

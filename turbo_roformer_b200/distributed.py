@@ -1,0 +1,105 @@
+"""Chunk-parallel separation over the GPUs of one node (one process per GPU, torch.distributed).
+
+A song's chunk list (the reference schedule, turbo_roformer/chunking.py:11-33) is split into contiguous
+shards, one per rank. Each rank runs its shard through its own model replica in batched forwards; the
+chunk outputs are then gathered to rank 0 in a single collective (NCCL over NVLink on GPUs, gloo on CPU
+for tests), and rank 0 applies the Hamming overlap-add in start order, so the result equals the
+single-device result bit for bit. There is no other collective.
+"""
+
+from __future__ import annotations
+
+from collections.abc import Callable
+
+import torch
+import torch.distributed as dist
+
+from .chunking import chunk_starts, hamming, step_for
+
+
+def shard_bounds(n_chunks: int, world: int) -> list[tuple[int, int]]:
+    """Contiguous [lo, hi) chunk ranges; the first n_chunks % world ranks take one extra chunk."""
+    q, r = divmod(n_chunks, world)
+    out, lo = [], 0
+    for k in range(world):
+        hi = lo + q + (1 if k < r else 0)
+        out.append((lo, hi))
+        lo = hi
+    return out
+
+
+def gather_chunks(local: torch.Tensor, counts: list[int], group=None) -> torch.Tensor | None:
+    """Single gather of per-rank chunk outputs (padded to the largest shard) to rank 0.
+
+    local: (max_count, 2, L) on this rank (rows past this rank's count are ignored).
+    Returns (sum(counts), 2, L) on rank 0, None elsewhere.
+    """
+    rank = dist.get_rank(group)
+    world = dist.get_world_size(group)
+    gl = [torch.empty_like(local) for _ in range(world)] if rank == 0 else None
+    dist.gather(local, gl, dst=0, group=group)
+    if rank != 0:
+        return None
+    return torch.cat([g[:c] for g, c in zip(gl, counts)], dim=0)
+
+
+def separate_sharded(
+    run_shard: Callable[[list[int], torch.Tensor], None],
+    n: int,
+    chunk: int,
+    overlap: float,
+    out_len: int,
+    device: torch.device,
+    ola: Callable[[torch.Tensor, list[int], int, int], torch.Tensor],
+    group=None,
+) -> torch.Tensor | None:
+    """Generic sharded overlap-add.
+
+    run_shard(starts, out): fill out[i] (2, out_len) with the model output of the chunk at starts[i].
+    ola(chunks, starts, C, n): weighted overlap-add on rank 0.
+    Returns (2, n) on rank 0, None on the other ranks.
+    """
+    rank = dist.get_rank(group)
+    world = dist.get_world_size(group)
+    C = min(chunk, n)
+    starts = chunk_starts(n, C, step_for(C, overlap))
+    bounds = shard_bounds(len(starts), world)
+    counts = [hi - lo for lo, hi in bounds]
+    lo, hi = bounds[rank]
+    local = torch.zeros(max(counts), 2, out_len, device=device, dtype=torch.float32)
+    if hi > lo:
+        run_shard(starts[lo:hi], local)
+    allc = gather_chunks(local, counts, group)
+    if rank != 0:
+        return None
+    return ola(allc, starts, C, n)
+
+
+def ola_torch(chunks: torch.Tensor, starts: list[int], C: int, n: int) -> torch.Tensor:
+    """Overlap-add in torch (any device), start order, used by the CPU (gloo) path."""
+    w = torch.from_numpy(hamming(C)).to(chunks.device)
+    result = torch.zeros(2, n, dtype=torch.float32, device=chunks.device)
+    weight = torch.zeros(n, dtype=torch.float32, device=chunks.device)
+    L = min(C, chunks.shape[-1])
+    for y, s in zip(chunks, starts):
+        result[:, s : s + L] += y[:, :L] * w[:L]
+        weight[s : s + L] += w[:L]
+    return result.div_(weight.clamp_(min=1e-10))
+
+
+def separate_song_cuda(sep, x: torch.Tensor, overlap: float = 2.0, group=None) -> torch.Tensor | None:
+    """Shard one song over the process group with CUDA models.
+
+    sep: a ``Separator`` (backend cuda) on this rank's GPU; x: (2, n) padded, gain-applied song on that GPU.
+    Returns the (2, n) instrumental on rank 0's GPU, None elsewhere.
+    """
+    from .chunking import ola_device, run_chunks
+
+    model = sep.net
+    C = min(sep.chunk, x.shape[1])
+
+    def run_shard(starts, out):
+        run_chunks(model, x, starts, C, sep.batch, out)
+
+    return separate_sharded(run_shard, x.shape[1], sep.chunk, overlap, model.output_length(C), x.device,
+                            lambda ch, st, c, n: ola_device(ch, st, c, n), group)

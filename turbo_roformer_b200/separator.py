@@ -1,0 +1,268 @@
+"""``Separator`` with ``backend="cuda"``: the reference's public API (turbo_roformer/separator.py:57-283)
+served by the B200 kernels.
+
+Same constructor shape, same ``separate`` / ``separate_file`` / ``n_chunks`` / ``from_module`` methods,
+same chunking, short-clip padding, peak normalisation to 0.9, Hamming overlap-add and
+vocals = mix - instrumental. Differences: ``backend`` is ``"cuda"`` (``"auto"`` means the same), the
+precision names the tensor-core operand type (``"fp16"`` default, ``"bf16"``), ``device`` picks the GPU
+and ``batch`` is how many chunks share one forward call. Weights are never downloaded by this package:
+a registry name resolves to a checkpoint already present in ``model_dir``.
+"""
+
+from __future__ import annotations
+
+import logging
+import os
+import threading
+import time
+from collections.abc import Callable
+from pathlib import Path
+from typing import Any
+
+import numpy as np
+import torch
+
+from . import audio
+from .backend import CudaBSRoformer
+from .chunking import chunk_starts, overlap_add_cuda, step_for
+from .config import RESURRECTION, infer_config
+
+log = logging.getLogger("turbo_roformer_b200")
+
+SR = 44100
+PEAK = 0.9
+BACKENDS = ("cuda", "auto")
+PRECISIONS = ("fp16", "bf16")
+
+# registry name -> (checkpoint file name, hop, dim_t) (turbo_roformer/registry.py:71-94)
+KNOWN_MODELS = {
+    "resurrection": ("bs_roformer_instrumental_resurrection_unwa.ckpt", 441, 1700),
+    "bs_roformer_instrumental_resurrection_unwa": ("bs_roformer_instrumental_resurrection_unwa.ckpt", 441, 1700),
+    "resurrection-inst": ("bs_roformer_instrumental_resurrection_unwa.ckpt", 441, 1700),
+}
+
+
+def default_model_dir() -> Path:
+    root = os.environ.get("TURBO_ROFORMER_HOME") or os.path.join(
+        os.environ.get("XDG_CACHE_HOME", os.path.expanduser("~/.cache")), "turbo-roformer"
+    )
+    return Path(root) / "models"
+
+
+def load_state_dict(path: str | os.PathLike) -> dict:
+    """Plain state dict, or one wrapped in ``state_dict`` / ``model`` (turbo_roformer/model.py:289-297)."""
+    sd = torch.load(str(path), map_location="cpu", weights_only=True)
+    if isinstance(sd, dict) and isinstance(sd.get("state_dict"), dict):
+        sd = sd["state_dict"]
+    elif isinstance(sd, dict) and isinstance(sd.get("model"), dict):
+        sd = sd["model"]
+    return {k: v.float() for k, v in sd.items()}
+
+
+class Separator:
+    """Vocal/instrumental separation with a BS-RoFormer model on a B200.
+
+    ``separate`` is serialised by an internal lock: an instance owns device work buffers, so concurrent
+    calls on the same instance wait for each other.
+    """
+
+    def __init__(
+        self,
+        model: str = "resurrection",
+        precision: str = "fp16",
+        threads: int | None = None,
+        model_dir: str | os.PathLike | None = None,
+        *,
+        backend: str = "cuda",
+        config: str | os.PathLike | None = None,
+        progress: bool = True,
+        device: int | None = None,
+        batch: int = 4,
+    ):
+        self._check_args(precision, backend)
+        t0 = time.perf_counter()
+        self.threads = threads
+        if threads:
+            torch.set_num_threads(int(threads))
+        sd, hop, dim_t, name = self._resolve(model, model_dir, config)
+        self.model_name = name
+        self._configure(sd, hop, dim_t, precision, device, batch)
+        self.load_s = time.perf_counter() - t0
+
+    # ------------------------------------------------------------------ construction helpers
+    @staticmethod
+    def _check_args(precision: str, backend: str) -> None:
+        if precision not in PRECISIONS:
+            raise ValueError(f"precision must be one of {PRECISIONS}")
+        if backend not in BACKENDS:
+            raise ValueError(f"backend must be one of {BACKENDS} (the CPU backends live in the reference package)")
+
+    @staticmethod
+    def _resolve(model, model_dir, config) -> tuple[dict, int, int, str]:
+        key = str(model).lower()
+        if key in KNOWN_MODELS:
+            fname, hop, dim_t = KNOWN_MODELS[key]
+            path = Path(model_dir).expanduser() / fname if model_dir else default_model_dir() / fname
+            if not path.exists():
+                raise FileNotFoundError(
+                    f"{path} not found: this backend does not download weights; place the checkpoint there "
+                    "or pass its path with config="
+                )
+            return load_state_dict(path), hop, dim_t, key
+        p = Path(str(model)).expanduser()
+        if not p.is_file():
+            raise KeyError(f"unknown model {model!r}; pass a registry name or a .ckpt path with config=")
+        if config is None:
+            raise ValueError("a custom checkpoint needs config=<yaml>")
+        import yaml
+
+        with open(config, encoding="utf-8") as f:
+            cfg = yaml.safe_load(f)
+        mcfg = cfg["model"]
+        hop = int(mcfg.get("stft_hop_length", 512))
+        dim_t = int(cfg.get("inference", {}).get("dim_t") or cfg.get("audio", {}).get("dim_t") or 801)
+        return load_state_dict(p), hop, dim_t, p.name
+
+    def _configure(self, sd, hop, dim_t, precision, device, batch) -> None:
+        cfg = infer_config(sd, hop=hop, dim_t=dim_t)
+        self.net = CudaBSRoformer(sd, cfg=cfg, device=device, precision=precision)
+        self.cfg = cfg
+        self.hop = hop
+        self.chunk = hop * (dim_t - 1)
+        self.backend, self.precision = "cuda", precision
+        self.batch = max(1, int(batch))
+        self._lock = threading.Lock()
+
+    @classmethod
+    def from_module(
+        cls,
+        net,
+        hop: int,
+        dim_t: int,
+        precision: str = "fp16",
+        backend: str = "cuda",
+        threads: int | None = None,
+        device: int | None = None,
+        batch: int = 4,
+    ) -> Separator:
+        """Wrap an already constructed BS-RoFormer module (or its state dict) (separator.py:160-179)."""
+        cls._check_args(precision, backend)
+        self = cls.__new__(cls)
+        self.threads = threads
+        if threads:
+            torch.set_num_threads(int(threads))
+        sd = net if isinstance(net, dict) else net.state_dict()
+        self.model_name = "custom"
+        self._configure(sd, hop, dim_t, precision, device, batch)
+        self.load_s = 0.0
+        return self
+
+    @classmethod
+    def from_state_dict(cls, sd: dict, hop: int = RESURRECTION.stft_hop_length, dim_t: int = RESURRECTION.dim_t,
+                        **kw) -> Separator:
+        return cls.from_module(sd, hop, dim_t, **kw)
+
+    # ------------------------------------------------------------------ separation
+    @property
+    def device(self) -> torch.device:
+        return self.net.device
+
+    def n_chunks(self, n_samples: int, overlap: float = 2.0) -> int:
+        C = min(self.chunk, n_samples)
+        return len(chunk_starts(n_samples, C, step_for(C, overlap)))
+
+    def prepare_44k(self, x: np.ndarray) -> tuple[np.ndarray, float]:
+        """Short-clip padding and peak gain (separator.py:190-197): returns (padded x * gain, gain)."""
+        n0 = x.shape[1]
+        if n0 < self.chunk and (n0 % self.hop or n0 < 3 * self.hop):
+            target = max(-(-n0 // self.hop) * self.hop, 3 * self.hop)
+            x = np.pad(x, ((0, 0), (0, target - n0)))
+        peak = float(np.abs(x).max())
+        gain = PEAK / peak if peak > PEAK else 1.0
+        return np.ascontiguousarray(x * np.float32(gain) if gain != 1.0 else x), gain
+
+    def separate_device(self, x: torch.Tensor, overlap: float = 2.0, progress=None) -> torch.Tensor:
+        """(2, n) float32 already on the model's GPU (padded and gain-applied) -> (2, n) on the GPU."""
+        return overlap_add_cuda(self.net, x, self.chunk, overlap, batch=self.batch, progress=progress)
+
+    @torch.inference_mode()
+    def _separate_44k(self, x: np.ndarray, overlap: float, progress) -> np.ndarray:
+        n0 = x.shape[1]
+        xp, gain = self.prepare_44k(x)
+        xt = torch.from_numpy(xp).to(self.device)
+        inst = self.separate_device(xt, overlap, progress).cpu()
+        if gain != 1.0:
+            inst.div_(gain)
+        return np.ascontiguousarray(inst.numpy()[:, :n0])
+
+    def separate(
+        self,
+        mix,
+        sr: int = SR,
+        overlap: float = 2.0,
+        progress: Callable[[int, int], None] | None = None,
+    ) -> np.ndarray:
+        """Instrumental as float32 (2, samples) at ``sr``; vocals = ``to_stereo(mix) - inst`` (separator.py:203-232)."""
+        if not overlap >= 1.0:
+            raise ValueError("overlap must be >= 1")
+        if int(sr) <= 0:
+            raise ValueError("sr must be positive")
+        sr = int(sr)
+        x = audio.to_stereo(audio.as_channels_first(mix))
+        n = x.shape[1]
+        if sr != SR:
+            x = audio.resample(x, sr, SR, length=max(1, round(n * SR / sr)))
+        with self._lock:
+            if self.threads:
+                torch.set_num_threads(int(self.threads))
+            inst = self._separate_44k(x, float(overlap), progress)
+        if sr != SR:
+            inst = audio.resample(inst, SR, sr, length=n)
+        return inst
+
+    def separate_file(
+        self,
+        in_path: str | os.PathLike,
+        out_dir: str | os.PathLike,
+        formats: tuple[str, ...] | list[str] = ("wav",),
+        overlap: float = 2.0,
+        progress: Callable[[int, int], None] | None = None,
+    ) -> dict[str, Any]:
+        """Write ``<stem>_instrumental.<fmt>`` and ``<stem>_vocals.<fmt>``; returns paths and timings
+        (separator.py:234-283)."""
+        for fmt in formats:
+            if fmt not in audio.output_formats():
+                raise ValueError(f"unsupported output format {fmt!r}")
+        t0 = time.perf_counter()
+        mix, sr = audio.load(in_path)
+        t1 = time.perf_counter()
+        stereo = audio.to_stereo(audio.as_channels_first(mix))
+        inst = self.separate(stereo, sr=sr, overlap=overlap, progress=progress)
+        vocals = stereo - inst
+        t2 = time.perf_counter()
+        out = Path(out_dir)
+        out.mkdir(parents=True, exist_ok=True)
+        stem = Path(in_path).stem
+        files: dict[str, str] = {}
+        for fmt in formats:
+            for name, data in (("instrumental", inst), ("vocals", vocals)):
+                p = out / f"{stem}_{name}.{fmt}"
+                audio.write(p, data, sr, fmt)
+                files[f"{name}.{fmt}"] = str(p)
+        t3 = time.perf_counter()
+        duration = stereo.shape[1] / sr
+        return dict(
+            instrumental=files[f"instrumental.{formats[0]}"],
+            vocals=files[f"vocals.{formats[0]}"],
+            files=files,
+            duration_s=duration,
+            sample_rate=sr,
+            n_chunks=self.n_chunks(round(stereo.shape[1] * SR / sr), overlap),
+            read_s=t1 - t0,
+            separate_s=t2 - t1,
+            write_s=t3 - t2,
+            wall_s=t3 - t0,
+            rtf=(t3 - t0) / duration,
+            backend=self.backend,
+            precision=self.precision,
+        )
