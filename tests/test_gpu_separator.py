@@ -1,0 +1,124 @@
+"""Separator API on the CUDA backend (the reference's tests/test_separator.py cases that need no resampler or
+sound files), checked against the reference's own Separator output on the small model."""
+
+from __future__ import annotations
+
+import threading
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import chunking_oracle, roformer_oracle
+from turbo_roformer_b200 import synthetic as S
+
+from .conftest import snr_db
+
+pytestmark = pytest.mark.gpu
+
+SR = 44100
+
+
+@pytest.fixture(scope="module")
+def sep(tiny_sd, tiny_cfg, cuda_device):
+    from turbo_roformer_b200.separator import Separator
+
+    return Separator.from_module(tiny_sd, tiny_cfg.stft_hop_length, tiny_cfg.dim_t, batch=3)
+
+
+def test_separate_matches_reference_separator(sep, golden_tiny):
+    mix = S.chunk_audio(44100, seed=7) * 3.0  # peak gain path
+    inst = sep.separate(mix, overlap=2.0)
+    assert inst.shape == mix.shape and inst.dtype == np.float32
+    assert snr_db(golden_tiny["separate_inst"], inst) >= 50.0
+
+
+def test_short_clip_matches_reference(sep, golden_tiny):
+    inst = sep.separate(S.chunk_audio(300, seed=8))
+    assert inst.shape == (2, 300)
+    assert snr_db(golden_tiny["separate_short_inst"], inst) >= 50.0
+
+
+def test_device_overlap_add_is_bit_identical_to_reference_loop(sep, tiny_cfg):
+    """Same chunk outputs -> the device overlap-add equals the reference's sequential loop exactly."""
+    from turbo_roformer_b200.chunking import chunk_starts, ola_device, step_for
+
+    mix = S.chunk_audio(3 * SR, seed=5)
+    xp, _ = sep.prepare_44k(mix)
+    x = torch.from_numpy(xp).cuda()
+    C = sep.chunk
+    starts = chunk_starts(x.shape[1], C, step_for(C, 2.0))
+    ys = sep.net.forward_device(torch.stack([x[:, s : s + C] for s in starts]))
+    dev = ola_device(ys, starts, C, x.shape[1]).cpu()
+    ref = chunking_oracle.ola_from_outputs(list(ys.cpu()), starts, x.shape[1], C)
+    assert torch.equal(dev, ref)
+
+
+@pytest.mark.parametrize("n", [1, 2, 127, 128, 383, 385, 16255, 16256, 16257])
+def test_short_and_boundary_lengths(sep, n):
+    mix = S.chunk_audio(max(n, 2), seed=n)[:, :n]
+    inst = sep.separate(mix)
+    assert inst.shape == (2, n)
+    assert np.isfinite(inst).all()
+
+
+def test_deterministic_and_mono(sep):
+    mix = S.chunk_audio(SR, seed=4)
+    np.testing.assert_array_equal(sep.separate(mix), sep.separate(mix))
+    mono = mix[:1]
+    a = sep.separate(mono[0])
+    np.testing.assert_array_equal(a, sep.separate(mono))
+    np.testing.assert_array_equal(a, sep.separate(np.repeat(mono, 2, axis=0)))
+
+
+def test_peak_normalisation_is_scale_invariant(sep):
+    mix = S.chunk_audio(SR, seed=12)
+    a = sep.separate(mix * 2.0) / 2.0
+    b = sep.separate(mix * 4.0) / 4.0
+    assert snr_db(a, b) > 100
+
+
+@pytest.mark.parametrize("overlap", [1.0, 1.5, 3.0])
+def test_overlaps_match_oracle(sep, tiny_sd, tiny_cfg, overlap):
+    mix = S.chunk_audio(SR, seed=13)
+    inst = sep.separate(mix, overlap=overlap)
+    ref = chunking_oracle.separate_44k(mix, sep.chunk, sep.hop, overlap,
+                                       lambda c: roformer_oracle.forward(c, tiny_sd, tiny_cfg))
+    assert snr_db(ref, inst) >= 50.0
+
+
+def test_progress_and_invalid_arguments(sep):
+    mix = S.chunk_audio(SR)
+    calls = []
+    sep.separate(mix, progress=lambda k, n: calls.append((k, n)))
+    n = sep.n_chunks(SR)
+    assert calls[-1] == (n, n) and all(b == n for _, b in calls)
+    with pytest.raises(ValueError):
+        sep.separate(mix, overlap=0.5)
+    with pytest.raises(ValueError):
+        sep.separate(mix, sr=0)
+    with pytest.raises(ValueError):
+        sep.separate(np.zeros((2, 10), np.int16))
+
+
+def test_concurrent_calls_are_serialised(sep):
+    mix = S.chunk_audio(SR, seed=14)
+    expected = sep.separate(mix)
+    results = [None] * 3
+
+    def work(i):
+        results[i] = sep.separate(mix)
+
+    ts = [threading.Thread(target=work, args=(i,)) for i in range(3)]
+    for t in ts:
+        t.start()
+    for t in ts:
+        t.join()
+    for r in results:
+        np.testing.assert_array_equal(r, expected)
+
+
+def test_vocals_identity(sep):
+    mix = S.chunk_audio(3 * SR, seed=9)
+    inst = sep.separate(mix)
+    np.testing.assert_allclose(inst + (mix - inst), mix, atol=1e-6)

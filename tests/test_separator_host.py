@@ -1,0 +1,82 @@
+"""Host-side Separator logic that needs no GPU: input validation, channel handling, padding and peak gain,
+and the loud failure when the CUDA backend is unavailable."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import chunking_oracle as O
+from turbo_roformer_b200 import audio
+from turbo_roformer_b200.separator import Separator
+
+
+@pytest.mark.parametrize(
+    "bad",
+    [
+        np.array([[0.0, np.nan, 0.0]] * 2, np.float32),
+        np.array([[0.0, np.inf, 0.0]] * 2, np.float32),
+        np.zeros((2, 0), np.float32),
+        np.zeros((2, 10), np.int16),
+        np.zeros((1000, 2), np.float32),
+        np.zeros((2, 2, 10), np.float32),
+    ],
+)
+def test_invalid_input_raises(bad):
+    with pytest.raises(ValueError):
+        audio.as_channels_first(bad)
+
+
+def test_downmix_keeps_centre():
+    rng = np.random.default_rng(2)
+    six = rng.standard_normal((6, 1000)).astype(np.float32)
+    centre_only = np.zeros_like(six)
+    centre_only[2] = six[2]
+    dm = audio.downmix_stereo(centre_only)
+    assert np.abs(dm).max() > 0.2 * np.abs(six[2]).max()
+    np.testing.assert_allclose(dm[0], dm[1])
+    assert audio.to_stereo(six).shape == (2, 1000)
+    mono = six[:1]
+    np.testing.assert_array_equal(audio.to_stereo(mono), np.repeat(mono, 2, axis=0))
+
+
+def _bare(chunk=16256, hop=128):
+    s = Separator.__new__(Separator)
+    s.chunk, s.hop = chunk, hop
+    return s
+
+
+@pytest.mark.parametrize("n", [1, 2, 127, 128, 383, 385, 16255, 16256, 16257])
+def test_short_clip_padding_and_gain_match_reference_rules(n):
+    rng = np.random.default_rng(n)
+    x = (3.0 * rng.standard_normal((2, n))).astype(np.float32)
+    s = _bare()
+    xp, gain = s.prepare_44k(x)
+    captured = {}
+
+    def run(c):
+        captured.setdefault("first", c.clone())
+        return c
+
+    O.separate_44k(x, s.chunk, s.hop, 2.0, run)  # the oracle pads/gains identically before its first chunk
+    assert xp.shape[1] >= n
+    first = captured["first"][0].numpy()
+    np.testing.assert_array_equal(xp[:, : first.shape[1]], first)
+    if np.abs(x).max() > 0.9:
+        assert gain == pytest.approx(0.9 / np.abs(x).max())
+
+
+def test_backend_and_precision_validation():
+    with pytest.raises(ValueError):
+        Separator._check_args("fp32", "cuda")
+    with pytest.raises(ValueError):
+        Separator._check_args("fp16", "torch")
+
+
+@pytest.mark.skipif(torch.cuda.is_available(), reason="checks the no-GPU failure mode")
+def test_cuda_backend_fails_loudly_without_gpu(tiny_sd):
+    from turbo_roformer_b200._lib import KernelUnavailable
+
+    with pytest.raises(KernelUnavailable):
+        Separator.from_module(tiny_sd, 128, 128)
