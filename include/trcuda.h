@@ -88,6 +88,21 @@ int trc_ola(const float* d_chunks, int64_t chunk_out_len, const int64_t* h_start
 
 const char* trc_last_error(void);
 
+/* Overlap-add that allocates nothing. No counterpart in the reference: it exists for callers that may
+ * not allocate device memory while they run (a host application capturing its processing into a CUDA
+ * graph, a plugin whose host owns all device memory, a real-time audio thread that must not enter the
+ * allocator). Same arguments, semantics and result as trc_ola, but the Hamming window and the chunk
+ * starts are staged in fixed arrays inside this library (one set per GPU that loads it, kept until the
+ * process exits: TRC_OLA_NOALLOC_MAX_CHUNK floats + TRC_OLA_NOALLOC_MAX_CHUNKS int64, about 8 MiB).
+ * Longer chunks or more chunks are rejected with TRC_E_INVALID. The first call on a device looks the
+ * arrays up (one-time set-up); make that first call before any stream capture. All calls share the
+ * arrays: calls that may overlap on the GPU (different streams, or different host threads on one
+ * device) race and must be serialised by the caller. */
+#define TRC_OLA_NOALLOC_MAX_CHUNK (1 << 21)
+#define TRC_OLA_NOALLOC_MAX_CHUNKS 8192
+int trc_ola_noalloc(const float* d_chunks, int64_t chunk_out_len, const int64_t* h_starts, int n_chunks,
+                    int64_t chunk, int64_t n, float* d_result, void* stream);
+
 /* ------------------------------------------------------------------ instrumentation
  * Per-section device timing, the counterpart of the reference's opt-in per-section profile
  * (FastBSRoformer.timer, turbo_roformer/fast.py:62-80; same section keys: stft, band_split, norm,

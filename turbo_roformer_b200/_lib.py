@@ -66,6 +66,7 @@ SIGNATURES = {
     "trc_check": (c_int, [c_vp, c_vp]),
     "trc_ola": (c_int, [c_vp, c_i64, c_vp, c_int, c_i64, c_i64, c_vp, c_vp]),
     "trc_last_error": (c_char_p, []),
+    "trc_ola_noalloc": (c_int, [c_vp, c_i64, c_vp, c_int, c_i64, c_i64, c_vp, c_vp]),
     "trc_profile": (c_int, [c_vp, c_int]),
     "trc_profile_read": (c_int, [c_vp, c_char_p, c_int]),
     "trc_launch_count": (ctypes.c_longlong, []),

@@ -37,6 +37,14 @@ int fail(int code, const char* fmt, ...) {
   return code;
 }
 
+}  // namespace
+
+namespace trc {
+int set_last_error(int code, const char* msg) { return fail(code, "%s", msg); }
+}  // namespace trc
+
+namespace {
+
 #define TRC_CUDA(call)                                                                              \
   do {                                                                                              \
     cudaError_t e_ = (call);                                                                        \

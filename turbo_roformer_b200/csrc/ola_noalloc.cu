@@ -1,0 +1,100 @@
+// trc_ola_noalloc: the chunk overlap-add for callers that cannot allocate device memory.
+//
+// trc_ola stages the Hamming window and the chunk starts in buffers it obtains with cudaMallocAsync.
+// Some callers cannot allow that: code running inside a captured CUDA graph region of a host
+// application, plugins whose host application owns all device memory through its own pool and forbids
+// driver allocations, or real-time audio hosts that must not take the allocator's locks on their
+// processing thread. For them this entry point keeps the two staging arrays in fixed, file-scope
+// device arrays of this library instead. They exist once per GPU that loads the library and stay
+// allocated until the process exits (8 MiB + 64 KiB per GPU).
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <mutex>
+
+#include "../../include/trcuda.h"
+#include "internal.h"
+
+namespace {
+
+constexpr int64_t kMaxChunkSamples = TRC_OLA_NOALLOC_MAX_CHUNK;   // Hamming window length limit
+constexpr int kMaxChunks = TRC_OLA_NOALLOC_MAX_CHUNKS;           // number of chunk starts limit
+constexpr int kMaxDevices = 64;
+constexpr int kHostBlock = 4096;  // window samples computed per host staging step
+
+static __device__ __align__(256) float g_ola_window[kMaxChunkSamples];
+static __device__ __align__(256) int64_t g_ola_starts[kMaxChunks];
+
+struct DeviceScratch {
+  float* window = nullptr;
+  int64_t* starts = nullptr;
+};
+
+std::mutex g_scratch_mu;
+DeviceScratch g_scratch[kMaxDevices];
+
+// One-time set-up per device (with that device current): translate the arrays' host-side names into
+// device addresses. Host code must never pass the array names themselves to a kernel.
+cudaError_t scratch_for_current_device(DeviceScratch* out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  DeviceScratch& s = g_scratch[dev];
+  if (!s.window) {
+    void* w = nullptr;
+    void* st = nullptr;
+    if ((e = cudaGetSymbolAddress(&w, g_ola_window)) != cudaSuccess) return e;
+    if ((e = cudaGetSymbolAddress(&st, g_ola_starts)) != cudaSuccess) return e;
+    s.window = static_cast<float*>(w);
+    s.starts = static_cast<int64_t*>(st);
+  }
+  *out = s;
+  return cudaSuccess;
+}
+
+}  // namespace
+
+namespace trc {
+int set_last_error(int code, const char* msg);  // api.cu
+}
+
+extern "C" int trc_ola_noalloc(const float* d_chunks, int64_t chunk_out_len, const int64_t* h_starts, int n_chunks,
+                               int64_t chunk, int64_t n, float* d_result, void* stream) {
+  if (!d_chunks || !h_starts || !d_result || n_chunks < 1 || chunk < 1 || n < 1 || chunk_out_len < 1 ||
+      chunk_out_len > chunk)
+    return trc::set_last_error(TRC_E_INVALID, "bad overlap-add arguments");
+  if (chunk > kMaxChunkSamples)
+    return trc::set_last_error(TRC_E_INVALID, "trc_ola_noalloc: chunk longer than TRC_OLA_NOALLOC_MAX_CHUNK samples");
+  if (n_chunks > kMaxChunks)
+    return trc::set_last_error(TRC_E_INVALID, "trc_ola_noalloc: more than TRC_OLA_NOALLOC_MAX_CHUNKS chunks");
+  for (int i = 0; i < n_chunks; ++i) {
+    if (h_starts[i] < 0 || h_starts[i] + chunk > n) return trc::set_last_error(TRC_E_INVALID, "chunk out of range");
+    if (i && h_starts[i] <= h_starts[i - 1]) return trc::set_last_error(TRC_E_INVALID, "starts must be increasing");
+  }
+  DeviceScratch s;
+  if (scratch_for_current_device(&s) != cudaSuccess)
+    return trc::set_last_error(TRC_E_CUDA, "cudaGetSymbolAddress failed for the overlap-add scratch");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // The window and the starts are fully rewritten by every call before the kernel reads them, so
+  // nothing needs clearing. The window is computed in float64 and rounded to float32 exactly like the
+  // allocating entry point, a block at a time through a stack buffer (no host allocation either).
+  float block[kHostBlock];
+  for (int64_t k0 = 0; k0 < chunk; k0 += kHostBlock) {
+    const int64_t m = chunk - k0 < kHostBlock ? chunk - k0 : kHostBlock;
+    for (int64_t k = 0; k < m; ++k) {
+      block[k] = chunk == 1 ? 1.0f
+                            : (float)(0.54 - 0.46 * std::cos(2.0 * M_PI * (double)(k0 + k) / (double)(chunk - 1)));
+    }
+    // pageable source: the copy is staged before cudaMemcpyAsync returns, so `block` can be reused
+    if (cudaMemcpyAsync(s.window + k0, block, sizeof(float) * m, cudaMemcpyHostToDevice, st) != cudaSuccess)
+      return trc::set_last_error(TRC_E_CUDA, "window upload failed");
+  }
+  if (cudaMemcpyAsync(s.starts, h_starts, sizeof(int64_t) * n_chunks, cudaMemcpyHostToDevice, st) != cudaSuccess)
+    return trc::set_last_error(TRC_E_CUDA, "starts upload failed");
+  trc::launch_chunk_ola(d_chunks, chunk_out_len, s.starts, n_chunks, s.window, n, d_result, st);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return trc::set_last_error(TRC_E_CUDA, cudaGetErrorString(e));
+  return TRC_OK;
+}
