@@ -94,6 +94,10 @@ int make_map(CUtensorMap* m, int precision, const void* ptr, int rank, const uin
   return TRC_OK;
 }
 
+// Cached variant for the forward path (keyed on everything that defines the map).
+int make_map_cached(trc_handle* h, CUtensorMap* m, const void* ptr, int rank, const uint64_t* dims,
+                    const uint64_t* strides_bytes, const uint32_t* box);
+
 // [rows][cols] with box (64, box_rows)
 int map_2d(CUtensorMap* m, int prec, const void* p, uint64_t cols, uint64_t rows, uint32_t box_rows) {
   const uint64_t dims[2] = {cols, rows};
@@ -189,6 +193,8 @@ struct trc_handle {
   DevBuf<float> xin, X, mask, frames;
   DevBuf<uint16_t> xn, Q, K, V, O, H;
   DevBuf<float> G;
+  // tensor maps by (pointer, precision, rank, dims, strides, box): work buffers are stable, so most hit
+  std::map<std::vector<uint64_t>, CUtensorMap> map_cache;
   // section timing (CUDA events on the launch stream, like the reference's per-section _Timer)
   bool timing = false;
   std::vector<cudaEvent_t> ev_pool;
@@ -241,6 +247,36 @@ struct Section {
     }
   }
 };
+
+int make_map_cached(trc_handle* h, CUtensorMap* m, const void* ptr, int rank, const uint64_t* dims,
+                    const uint64_t* strides_bytes, const uint32_t* box) {
+  std::vector<uint64_t> key;
+  key.reserve(16);
+  key.push_back(reinterpret_cast<uint64_t>(ptr));
+  key.push_back((uint64_t)h->prec);
+  key.push_back((uint64_t)rank);
+  for (int i = 0; i < rank; ++i) key.push_back(dims[i]);
+  for (int i = 0; i < rank - 1; ++i) key.push_back(strides_bytes[i]);
+  for (int i = 0; i < rank; ++i) key.push_back(box[i]);
+  auto it = h->map_cache.find(key);
+  if (it != h->map_cache.end()) {
+    *m = it->second;
+    return TRC_OK;
+  }
+  const int rc = make_map(m, h->prec, ptr, rank, dims, strides_bytes, box);
+  if (rc == TRC_OK) {
+    if (h->map_cache.size() > 4096) h->map_cache.clear();
+    h->map_cache[key] = *m;
+  }
+  return rc;
+}
+
+int map_2d_cached(trc_handle* h, CUtensorMap* m, const void* p, uint64_t cols, uint64_t rows, uint32_t box_rows) {
+  const uint64_t dims[2] = {cols, rows};
+  const uint64_t st[1] = {cols * 2};
+  const uint32_t box[2] = {64, box_rows};
+  return make_map_cached(h, m, p, 2, dims, st, box);
+}
 
 const std::vector<float>* param(trc_handle* h, const std::string& name, size_t numel) {
   auto it = h->params.find(name);
@@ -311,7 +347,7 @@ GemmArgs dense_args(trc_handle* h, int64_t rows, int n_cols, int k) {
   a.n_tiles = (n_cols + 255) / 256;
   a.num_tiles = m_tiles * a.n_tiles;
   a.k_blocks = k / 64;
-  a.a_mode = 0;
+  a.a_mode = trc::A_ROWS;
   a.M = (int)rows;
   a.N = n_cols;
   a.n_groups = 0;
@@ -320,18 +356,56 @@ GemmArgs dense_args(trc_handle* h, int64_t rows, int n_cols, int k) {
   return a;
 }
 
+// Q/K/V tensor maps of the attention layout. time: 3-D (64, T, B*F*8), box (64, 128, 1) = 128 frames of
+// one (batch, band, head) sequence; freq: 4-D (64, F, 8, B*T), box (64, 64, 1, 2) = two frames' band
+// sequences of one head (rows f >= F are clipped / zero-filled).
+int qkv_map(trc_handle* h, CUtensorMap* m, const void* p, int mode, int B, int T) {
+  const int F = h->nb;
+  if (mode == 0) {
+    const uint64_t dims[3] = {64, (uint64_t)T, (uint64_t)B * F * 8};
+    const uint64_t st[2] = {128, (uint64_t)T * 128};
+    const uint32_t box[3] = {64, 128, 1};
+    return make_map_cached(h, m, p, 3, dims, st, box);
+  }
+  const uint64_t dims[4] = {64, (uint64_t)F, 8, (uint64_t)B * T};
+  const uint64_t st[3] = {128, (uint64_t)F * 128, (uint64_t)F * 8 * 128};
+  const uint32_t box[4] = {64, 64, 1, 2};
+  return make_map_cached(h, m, p, 4, dims, st, box);
+}
+
 int run_qkv(trc_handle* h, int layer, const void* xn, int B, int T, void* Q, void* K, void* V, float* G,
             cudaStream_t st) {
   const int mode = layer & 1;
-  const int L = mode == 0 ? T : h->nb;
+  const int F = h->nb;
+  const int L = mode == 0 ? T : F;
+  if (F > 64) return fail(TRC_E_INVALID, "at most 64 bands are supported");
   Tables* tab = get_tables(h, mode, L);
   if (!tab) return TRC_E_CUDA;
-  const int64_t rows = (int64_t)B * T * h->nb;
   LayerDev& lw = *h->layers[layer];
-  CUtensorMap ma;
-  int rc = map_2d(&ma, h->prec, xn, 256, (uint64_t)rows, 128);
-  if (rc) return rc;
-  GemmArgs a = dense_args(h, rows, 1544, 256);
+  CUtensorMap ma, mo[3];
+  int rc;
+  GemmArgs a = dense_args(h, 1, 1544, 256);
+  if (mode == 0) {  // A rows: 128 consecutive frames of one band, xn viewed as (k, band, frame, batch)
+    const uint64_t dims[4] = {256, (uint64_t)F, (uint64_t)T, (uint64_t)B};
+    const uint64_t strides[3] = {512, (uint64_t)F * 512, (uint64_t)T * F * 512};
+    const uint32_t box[4] = {64, 1, 128, 1};
+    if ((rc = make_map_cached(h, &ma, xn, 4, dims, strides, box))) return rc;
+    a.a_mode = trc::A_TIME_SEQ;
+    a.M = T;
+    a.m_tiles = (T + 127) / 128;
+    a.num_tiles = B * F * a.m_tiles * a.n_tiles;
+  } else {  // A rows: two frames x 64 band slots, xn viewed as (k, band, frame)
+    const uint64_t dims[3] = {256, (uint64_t)F, (uint64_t)B * T};
+    const uint64_t strides[2] = {512, (uint64_t)F * 512};
+    const uint32_t box[3] = {64, 64, 2};
+    if ((rc = make_map_cached(h, &ma, xn, 3, dims, strides, box))) return rc;
+    a.a_mode = trc::A_FREQ_PAIR;
+    a.M = B * T;
+    a.num_tiles = ((B * T + 1) / 2) * a.n_tiles;
+  }
+  if ((rc = qkv_map(h, &mo[0], Q, mode, B, T)) || (rc = qkv_map(h, &mo[1], K, mode, B, T)) ||
+      (rc = qkv_map(h, &mo[2], V, mode, B, T)))
+    return rc;
   a.out0 = Q;
   a.out1 = K;
   a.out2 = V;
@@ -340,9 +414,8 @@ int run_qkv(trc_handle* h, int layer, const void* xn, int B, int T, void* Q, voi
   a.cos_tab = tab->cos_t.p;
   a.sin_tab = tab->sin_t.p;
   a.T = T;
-  a.F = h->nb;
-  a.mode = mode;
-  return check_launch(trc::launch_gemm(trc::EPI_QKV, h->prec, ma, lw.m_wqkv, a, h->num_sms, st), "qkv gemm");
+  a.F = F;
+  return check_launch(trc::launch_gemm(trc::EPI_QKV, h->prec, ma, lw.m_wqkv, mo, a, h->num_sms, st), "qkv gemm");
 }
 
 int run_attention(trc_handle* h, int mode, const void* Q, const void* K, const void* V, const float* G, void* O,
@@ -381,8 +454,8 @@ int run_attention(trc_handle* h, int mode, const void* Q, const void* K, const v
   strides[1] = (uint64_t)a.L * 128;
   CUtensorMap mq, mk, mv;
   int rc;
-  if ((rc = make_map(&mq, h->prec, Q, 3, dims, strides, box)) || (rc = make_map(&mk, h->prec, K, 3, dims, strides, box)) ||
-      (rc = make_map(&mv, h->prec, V, 3, dims, strides, box)))
+  if ((rc = make_map_cached(h, &mq, Q, 3, dims, strides, box)) || (rc = make_map_cached(h, &mk, K, 3, dims, strides, box)) ||
+      (rc = make_map_cached(h, &mv, V, 3, dims, strides, box)))
     return rc;
   return check_launch(trc::launch_attention(h->prec, mq, mk, mv, a, st), "attention");
 }
@@ -392,26 +465,32 @@ int run_res_norm(trc_handle* h, int layer, int which, const void* A, float* X, v
   LayerDev& lw = *h->layers[layer];
   const int k = which == 0 ? 512 : h->ff;
   CUtensorMap ma;
-  int rc = map_2d(&ma, h->prec, A, (uint64_t)k, (uint64_t)rows, 128);
+  int rc = map_2d_cached(h, &ma, A, (uint64_t)k, (uint64_t)rows, 128);
   if (rc) return rc;
   GemmArgs a = dense_args(h, rows, 256, k);
   a.out0 = X;
   a.out1 = xn;
   a.bias = which == 0 ? nullptr : lw.b2.p;
-  return check_launch(trc::launch_gemm(trc::EPI_RESNORM, h->prec, ma, which == 0 ? lw.m_wo : lw.m_w2, a, h->num_sms, st),
-                      "res-norm gemm");
+  const CUtensorMap mo[3] = {ma, ma, ma};  // unused by this epilogue
+  return check_launch(
+      trc::launch_gemm(trc::EPI_RESNORM, h->prec, ma, which == 0 ? lw.m_wo : lw.m_w2, mo, a, h->num_sms, st),
+      "res-norm gemm");
 }
 
 int run_gelu(trc_handle* h, int layer, const void* xn, void* H, int64_t rows, cudaStream_t st) {
   LayerDev& lw = *h->layers[layer];
   CUtensorMap ma;
-  int rc = map_2d(&ma, h->prec, xn, 256, (uint64_t)rows, 128);
+  int rc = map_2d_cached(h, &ma, xn, 256, (uint64_t)rows, 128);
   if (rc) return rc;
+  CUtensorMap mo[3];
+  if ((rc = map_2d_cached(h, &mo[0], H, (uint64_t)h->ff, (uint64_t)rows, 128))) return rc;
+  mo[1] = mo[0];
+  mo[2] = mo[0];
   GemmArgs a = dense_args(h, rows, h->ff, 256);
   a.out0 = H;
   a.bias = lw.b1.p;
   a.ld_out = h->ff;
-  return check_launch(trc::launch_gemm(trc::EPI_GELU, h->prec, ma, lw.m_w1, a, h->num_sms, st), "gelu gemm");
+  return check_launch(trc::launch_gemm(trc::EPI_GELU, h->prec, ma, lw.m_w1, mo, a, h->num_sms, st), "gelu gemm");
 }
 
 int run_mask(trc_handle* h, const void* xn, int B, int T, float* mask, void* hid, cudaStream_t st) {
@@ -425,11 +504,20 @@ int run_mask(trc_handle* h, const void* xn, int B, int T, float* mask, void* hid
     const uint64_t dims[3] = {256, (uint64_t)F, (uint64_t)BT};
     const uint64_t strides[2] = {512, (uint64_t)F * 512};
     const uint32_t box[3] = {64, 1, 128};
-    if ((rc = make_map(&ma, h->prec, xn, 3, dims, strides, box))) return rc;
+    if ((rc = make_map_cached(h, &ma, xn, 3, dims, strides, box))) return rc;
+    CUtensorMap mo[3];
+    {
+      const uint64_t odims[3] = {(uint64_t)h->hidden, (uint64_t)BT, (uint64_t)F};
+      const uint64_t ostr[2] = {(uint64_t)h->hidden * 2, (uint64_t)BT * h->hidden * 2};
+      const uint32_t obox[3] = {64, 128, 1};
+      if ((rc = make_map_cached(h, &mo[0], hid, 3, odims, ostr, obox))) return rc;
+      mo[1] = mo[0];
+      mo[2] = mo[0];
+    }
     GemmArgs a;
     std::memset(&a, 0, sizeof(a));
     a.k_blocks = 4;
-    a.a_mode = 1;
+    a.a_mode = trc::A_GROUP_ROWS;
     a.M = BT;
     a.n_groups = F;
     const int nt = (h->hidden + 255) / 256;
@@ -447,7 +535,7 @@ int run_mask(trc_handle* h, const void* xn, int B, int T, float* mask, void* hid
     a.bias = h->mk_b1.p;
     a.ld_out = h->hidden;
     a.err = h->err.p;
-    if ((rc = check_launch(trc::launch_gemm(trc::EPI_MASK_TANH, h->prec, ma, h->m_mk_w1, a, h->num_sms, st),
+    if ((rc = check_launch(trc::launch_gemm(trc::EPI_MASK_TANH, h->prec, ma, h->m_mk_w1, mo, a, h->num_sms, st),
                            "mask layer 1")))
       return rc;
   }
@@ -457,11 +545,12 @@ int run_mask(trc_handle* h, const void* xn, int B, int T, float* mask, void* hid
     const uint64_t dims[3] = {(uint64_t)h->hidden, (uint64_t)BT, (uint64_t)F};
     const uint64_t strides[2] = {(uint64_t)h->hidden * 2, (uint64_t)BT * h->hidden * 2};
     const uint32_t box[3] = {64, 128, 1};
-    if ((rc = make_map(&ma, h->prec, hid, 3, dims, strides, box))) return rc;
+    if ((rc = make_map_cached(h, &ma, hid, 3, dims, strides, box))) return rc;
+    const CUtensorMap mo[3] = {ma, ma, ma};  // unused by this epilogue
     GemmArgs a;
     std::memset(&a, 0, sizeof(a));
     a.k_blocks = h->hidden / 64;
-    a.a_mode = 2;
+    a.a_mode = trc::A_ROWS_GROUP;
     a.M = BT;
     a.n_groups = F;
     int acc = 0;
@@ -481,7 +570,7 @@ int run_mask(trc_handle* h, const void* xn, int B, int T, float* mask, void* hid
     a.bias = h->mk_b2.p;
     a.ld_out = h->width;
     a.err = h->err.p;
-    if ((rc = check_launch(trc::launch_gemm(trc::EPI_MASK_GLU, h->prec, ma, h->m_mk_w2, a, h->num_sms, st),
+    if ((rc = check_launch(trc::launch_gemm(trc::EPI_MASK_GLU, h->prec, ma, h->m_mk_w2, mo, a, h->num_sms, st),
                            "mask layer 2")))
       return rc;
   }
@@ -791,6 +880,12 @@ int trc_profile(trc_handle* h, int enable) {
   h->ev_pending.clear();
   h->section.clear();
   h->timing = enable != 0;
+  // create the events up front so the timed region does not pay for cudaEventCreate
+  while (h->timing && h->ev_pool.size() < 4096) {
+    cudaEvent_t e = nullptr;
+    TRC_CUDA(cudaEventCreate(&e));
+    h->ev_pool.push_back(e);
+  }
   return TRC_OK;
 }
 

@@ -1,13 +1,16 @@
 // Persistent tcgen05 GEMM  D[128 x BN] = A[128 x K] * B[BN x K]^T  with fused epilogues.
 //
-// Roles (192 threads):  warp 0 = TMA producer, warp 1 = MMA issuer + TMEM owner, warps 2-5 = epilogue.
+// Roles (320 threads): warp 0 = TMA producer, warp 1 = MMA issuer + TMEM owner, warps 2-9 = epilogue.
 // A and B are K-major 16-bit tiles (128-byte swizzle) streamed through a STAGES-deep shared-memory ring;
 // the accumulator lives in TMEM, double buffered (2 x BN columns) so the epilogue of tile i overlaps the
-// MMAs of tile i+1. Each epilogue thread owns one output row (TMEM lane), which makes row-wise epilogues
-// (residual add + L2 norm over the 256 features of a token) thread-local.
+// MMAs of tile i+1. Epilogue warp w reads TMEM lane quarter (w % 4) and one half of the columns, so
+// two warps share each SM sub-partition. 16-bit outputs are written through 128-byte-swizzled shared
+// staging slabs (128 rows x 64 columns) and stored with TMA, so global writes are whole lines and
+// asynchronous; the fp32 residual stream is updated by warp-cooperative coalesced row segments.
 //
 // Epilogues (the reference kernels they replace, LoggeL/turbo-roformer src/turbo_roformer/csrc/kernels.cpp):
-//   EPI_QKV       qkv_rope_gemm (:442-540): rotary on q,k in fp32, scatter to the attention layout, sigmoid gates
+//   EPI_QKV       qkv_rope_gemm (:442-540): rotary on q,k in fp32, Q/K/V stored per head as TMA boxes of
+//                 the attention layout, sigmoid gates (16-column tile)
 //   EPI_RESNORM   gemm_res_norm (:543-586): X += acc (+ bias); xn = X / max(|X|, eps)
 //   EPI_GELU      gemm_gelu (:610-642):     H = gelu_erf(acc + b)
 //   EPI_MASK_TANH mask MLP layer 1 (fast.py:354):  tanh(acc + b1) per band
@@ -20,20 +23,34 @@ namespace trc {
 
 enum EpiKind : int { EPI_QKV = 0, EPI_RESNORM = 1, EPI_GELU = 2, EPI_MASK_TANH = 3, EPI_MASK_GLU = 4 };
 
+// How a tile's 128 A rows are addressed.
+enum AMode : int {
+  A_ROWS = 0,        // 2-D [rows][K]: 128 consecutive rows
+  A_GROUP_ROWS = 1,  // 3-D (K, group, rows): rows of one group (mask layer 1: one band of every frame)
+  A_ROWS_GROUP = 2,  // 3-D (K, rows, group): group-major storage (mask layer 2)
+  A_TIME_SEQ = 3,    // 4-D (K, band, frame, batch): 128 consecutive frames of one band (time qkv)
+  A_FREQ_PAIR = 4,   // 3-D (K, band, frame): two frames x 64 band slots (freq qkv)
+};
+
 constexpr int kGemmBM = 128;
 constexpr int kGemmBK = 64;
-constexpr int kGemmThreads = 192;
+constexpr int kEpiWarps = 8;
+constexpr int kGemmThreads = 64 + 32 * kEpiWarps;
 constexpr int kMaxGroups = 64;
+constexpr int kSlabBytes = 128 * 128;  // 128 rows x 64 16-bit columns
 
 struct GemmArgs {
   // ---- schedule
   int num_tiles;
   int k_blocks;   // K / 64
-  int a_mode;     // 0: A map 2D (k, row); 1: 3D (k, group, row); 2: 3D (k, row, group)
-  int M;          // valid rows (per group when grouped)
-  int n_tiles;    // dense: N tiles per M tile
-  int N;          // dense: valid columns
-  int n_groups;   // 0 = dense
+  int a_mode;     // AMode
+  int M;          // valid rows: rows (dense), rows per group (grouped), T (time qkv), B*T (freq qkv)
+  int n_tiles;    // N tiles per M tile (dense and qkv)
+  int N;          // valid columns (dense and qkv)
+  int m_tiles;    // time qkv: M tiles per (batch, band)
+  int F;          // bands (qkv)
+  int T;          // frames per chunk (qkv)
+  int n_groups;   // grouped GEMMs: number of groups (0 otherwise)
   int g_tile_start[kMaxGroups + 1];
   int g_ntiles[kMaxGroups];
   int g_brow[kMaxGroups];    // first B row of the group
@@ -48,39 +65,79 @@ struct GemmArgs {
   const float* bias2;  // qkv: gate bias [8]
   const float* cos_tab;
   const float* sin_tab;
-  int T, F, mode, ld_out;
+  int ld_out;
   float eps;
   int* err;
 };
 
 struct TileCoord {
   int m0, n0, group, b_row, n_valid, n_mma;
+  int a1, a2, a3;  // TMA coordinates of A after the K coordinate
+  int b, f;        // time qkv: batch item and band of the tile
 };
 
 template <int BN>
 __device__ __forceinline__ TileCoord gemm_decode(const GemmArgs& a, int tile) {
   TileCoord c;
-  if (a.n_groups == 0) {
-    const int mt = tile / a.n_tiles, nt = tile - mt * a.n_tiles;
-    c.group = 0;
-    c.m0 = mt * kGemmBM;
-    c.n0 = nt * BN;
-    c.b_row = c.n0;
-    c.n_valid = min(BN, a.N - c.n0);
-  } else {
+  c.group = 0;
+  c.b = 0;
+  c.f = 0;
+  c.a3 = 0;
+  int nt;
+  if (a.n_groups > 0) {
     int g = 0;
     while (g + 1 < a.n_groups && tile >= a.g_tile_start[g + 1]) ++g;
     const int local = tile - a.g_tile_start[g];
-    const int mt = local / a.g_ntiles[g], nt = local - mt * a.g_ntiles[g];
+    const int mt = local / a.g_ntiles[g];
+    nt = local - mt * a.g_ntiles[g];
     c.group = g;
     c.m0 = mt * kGemmBM;
     c.n0 = nt * BN;
     c.b_row = a.g_brow[g] + c.n0;
     c.n_valid = min(BN, a.g_ncols[g] - c.n0);
+    if (a.a_mode == A_GROUP_ROWS) {
+      c.a1 = g;
+      c.a2 = c.m0;
+    } else {
+      c.a1 = c.m0;
+      c.a2 = g;
+    }
+  } else if (a.a_mode == A_TIME_SEQ) {
+    const int per = a.m_tiles * a.n_tiles;
+    const int bf = tile / per;
+    const int rem = tile - bf * per;
+    const int mt = rem / a.n_tiles;
+    nt = rem - mt * a.n_tiles;
+    c.b = bf / a.F;
+    c.f = bf - c.b * a.F;
+    c.m0 = mt * kGemmBM;  // first frame
+    c.n0 = nt * BN;
+    c.b_row = c.n0;
+    c.n_valid = min(BN, a.N - c.n0);
+    c.a1 = c.f;
+    c.a2 = c.m0;
+    c.a3 = c.b;
+  } else {
+    const int mt = tile / a.n_tiles;
+    nt = tile - mt * a.n_tiles;
+    c.m0 = a.a_mode == A_FREQ_PAIR ? 2 * mt : mt * kGemmBM;  // freq: first frame of the pair
+    c.n0 = nt * BN;
+    c.b_row = c.n0;
+    c.n_valid = min(BN, a.N - c.n0);
+    if (a.a_mode == A_FREQ_PAIR) {
+      c.a1 = 0;
+      c.a2 = c.m0;
+    } else {
+      c.a1 = c.m0;
+      c.a2 = 0;
+    }
   }
   c.n_mma = (c.n_valid + 15) & ~15;
   return c;
 }
+
+__device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + __expf(-x)); }
+__device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
 
 template <typename TIn>
 __device__ __forceinline__ void store32(TIn* dst, const float (&v)[32]) {
@@ -96,93 +153,158 @@ __device__ __forceinline__ void store32(TIn* dst, const float (&v)[32]) {
   }
 }
 
-__device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + __expf(-x)); }
-__device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
+// Row r of a [128][64] 16-bit slab in the 128-byte-swizzled layout TMA expects (16-byte chunk c of
+// row r lives at chunk c ^ (r % 8)); conflict-free for 32 consecutive rows.
+template <typename TIn>
+__device__ __forceinline__ void stage_slab_row(uint8_t* slab, int r, const float (&v0)[32], const float (&v1)[32]) {
+  uint32_t p[32];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    p[i] = OperandType<TIn>::pack2(v0[2 * i], v0[2 * i + 1]);
+    p[16 + i] = OperandType<TIn>::pack2(v1[2 * i], v1[2 * i + 1]);
+  }
+  uint8_t* row = slab + r * 128;
+#pragma unroll
+  for (int c = 0; c < 8; ++c)
+    *reinterpret_cast<uint4*>(row + ((c ^ (r & 7)) << 4)) = make_uint4(p[4 * c], p[4 * c + 1], p[4 * c + 2], p[4 * c + 3]);
+}
+
+// Per-thread epilogue context.
+struct EpiCtx {
+  uint32_t taddr;  // TMEM address: this warp's lane quarter, accumulator buffer column 0
+  int row;         // tile row (TMEM lane) of this thread
+  int lane, quarter, ewarp, hf;
+  bool leader;     // issues the TMA stores of its column half
+  uint8_t* slabs;  // 4 staging slabs: [half][2]
+  float* scratch;  // same memory, used by the residual-norm epilogue
+  int slot;        // next slab slot of this half (alternates 0, 1)
+};
+
+// Before writing a slab: the store previously issued from it must have finished reading.
+__device__ __forceinline__ uint8_t* slab_acquire(EpiCtx& e) {
+  if (e.leader) bulk_wait_read<1>();
+  named_bar(1 + e.hf, 128);
+  return e.slabs + (e.hf * 2 + e.slot) * kSlabBytes;
+}
+// After writing: make the slab visible to the async proxy, then the leader stores it.
+__device__ __forceinline__ void slab_release(EpiCtx& e) {
+  fence_async_smem();
+  named_bar(1 + e.hf, 128);
+  e.slot ^= 1;
+}
 
 // ------------------------------------------------------------------------------------------------ epilogues
-// taddr: TMEM address of (this thread's lane, column 0 of the accumulator buffer). row valid iff m < M.
-template <int BN, typename TIn>
-__device__ __forceinline__ void epi_qkv(const GemmArgs& a, const TileCoord& tc, uint32_t taddr, int m, bool valid) {
-  const int TF = a.T * a.F;
-  const int b = m / TF;
-  const int r = m - b * TF;
-  const int t = r / a.F;
-  const int f = r - t * a.F;
-  int pos, L, bh0;
-  if (a.mode == 0) {
-    pos = t; L = a.T; bh0 = (b * a.F + f) * 8;
-  } else {
-    pos = f; L = a.F; bh0 = (b * a.T + t) * 8;
+__device__ __forceinline__ bool qkv_token(const GemmArgs& a, const TileCoord& tc, int r, int* token) {
+  if (a.a_mode == A_TIME_SEQ) {
+    const int t = tc.m0 + r;
+    *token = (tc.b * a.T + t) * a.F + tc.f;
+    return t < a.T;
   }
-  if (tc.n0 >= 1536) {  // gate columns: sigmoid(x . Wg + bg) -> G[token][8]
-    float v[16];
-    tmem_ld16(taddr, v);
-    if (valid) {
-      float g[8];
+  const int bt = tc.m0 + (r >> 6);
+  const int f = r & 63;
+  *token = bt * a.F + f;
+  return f < a.F && bt < a.M;
+}
+
+__device__ __forceinline__ void rotate32(float (&v)[32], const float* cs, const float* sn) {
+  // interleaved pairs (2j, 2j+1) rotated by the angle of pair j: x0 c - x1 s, x1 c + x0 s
 #pragma unroll
-      for (int h = 0; h < 8; ++h) g[h] = sigmoidf_(v[h] + a.bias2[h]);
-      float4* G = reinterpret_cast<float4*>(static_cast<float*>(a.out3) + (size_t)m * 8);
-      G[0] = make_float4(g[0], g[1], g[2], g[3]);
-      G[1] = make_float4(g[4], g[5], g[6], g[7]);
+  for (int q = 0; q < 4; ++q) {
+    const float4 c4 = reinterpret_cast<const float4*>(cs)[q];
+    const float4 s4 = reinterpret_cast<const float4*>(sn)[q];
+    const float cc[4] = {c4.x, c4.y, c4.z, c4.w};
+    const float ss[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int j = q * 4 + e;
+      const float x0 = v[2 * j], x1 = v[2 * j + 1];
+      v[2 * j] = x0 * cc[e] - x1 * ss[e];
+      v[2 * j + 1] = x1 * cc[e] + x0 * ss[e];
     }
-    return;
-  }
-  const int part = tc.n0 >> 9;          // 0 q, 1 k, 2 v
-  const int h0 = (tc.n0 & 511) >> 6;    // first head of this tile
-  TIn* base = static_cast<TIn*>(part == 0 ? a.out0 : part == 1 ? a.out1 : a.out2);
-#pragma unroll 1
-  for (int c = 0; c < BN / 32; ++c) {
-    float v[32];
-    tmem_ld32(taddr + c * 32, v);
-    const int h = h0 + (c >> 1);
-    const int d0 = (c & 1) * 32;
-    if (part < 2 && valid) {
-      const float4* cp = reinterpret_cast<const float4*>(a.cos_tab + (size_t)pos * 32 + (d0 >> 1));
-      const float4* sp = reinterpret_cast<const float4*>(a.sin_tab + (size_t)pos * 32 + (d0 >> 1));
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float4 cs = cp[q], sn = sp[q];
-        const float cc[4] = {cs.x, cs.y, cs.z, cs.w};
-        const float ss[4] = {sn.x, sn.y, sn.z, sn.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int i = q * 4 + e;
-          const float x0 = v[2 * i], x1 = v[2 * i + 1];
-          v[2 * i] = x0 * cc[e] - x1 * ss[e];
-          v[2 * i + 1] = x1 * cc[e] + x0 * ss[e];
-        }
-      }
-    }
-    if (valid) store32<TIn>(base + ((size_t)(bh0 + h) * L + pos) * 64 + d0, v);
   }
 }
 
-// Residual add + row L2 norm, warp-cooperative: the warp's 32 rows x 256 columns are moved through a
-// padded shared-memory transpose 32 columns at a time, so X and xn are read and written as coalesced
-// 128-byte row segments (one row per instruction, all 32 rows' loads in flight before any store).
-// Per-lane partial sums of squares (one per row) are combined with a 31-shuffle transpose-reduce that
-// leaves the total of row `lane` in lane `lane`.
 template <int BN, typename TIn>
-__device__ __forceinline__ void epi_resnorm(const GemmArgs& a, uint32_t taddr, int row0, int lane,
-                                            float* stage) {
+__device__ __forceinline__ void epi_qkv(const GemmArgs& a, const TileCoord& tc, EpiCtx& e, const CUtensorMap* mq,
+                                        const CUtensorMap* mk, const CUtensorMap* mv) {
+  const int r = e.row;
+  if (tc.n0 >= 1536) {  // gate columns (16-wide MMA): half 0 holds them
+    if (e.hf == 0) {
+      float v[16];
+      tmem_ld16(e.taddr, v);
+      int token;
+      if (qkv_token(a, tc, r, &token)) {
+        float g[8];
+#pragma unroll
+        for (int h = 0; h < 8; ++h) g[h] = sigmoidf_(v[h] + a.bias2[h]);
+        float4* G = reinterpret_cast<float4*>(static_cast<float*>(a.out3) + (size_t)token * 8);
+        G[0] = make_float4(g[0], g[1], g[2], g[3]);
+        G[1] = make_float4(g[4], g[5], g[6], g[7]);
+      }
+    }
+    return;
+  }
+  const bool time = a.a_mode == A_TIME_SEQ;
+  const int part = tc.n0 >> 9;  // 0 q, 1 k, 2 v
+  const CUtensorMap* map = part == 0 ? mq : part == 1 ? mk : mv;
+  const int L = time ? a.T : a.F;
+  int pos = time ? tc.m0 + r : (r & 63);
+  pos = min(pos, L - 1);  // rows past the sequence end are clipped by the store; keep the table read in range
+  const float* cs = a.cos_tab + (size_t)pos * 32;
+  const float* sn = a.sin_tab + (size_t)pos * 32;
+#pragma unroll 1
+  for (int hh = 0; hh < 2; ++hh) {
+    const int hc = e.hf * 2 + hh;                    // head within the tile
+    const int h = ((tc.n0 & 511) >> 6) + hc;         // head index 0..7
+    uint8_t* slab = slab_acquire(e);
+    float v0[32], v1[32];
+    tmem_ld32(e.taddr + hc * 64, v0);
+    tmem_ld32(e.taddr + hc * 64 + 32, v1);
+    if (part < 2) {
+      rotate32(v0, cs, sn);
+      rotate32(v1, cs + 16, sn + 16);
+    }
+    stage_slab_row<TIn>(slab, r, v0, v1);
+    slab_release(e);
+    if (e.leader) {
+      if (time)
+        tma_store_3d(map, slab, 0, tc.m0, (tc.b * a.F + tc.f) * 8 + h);
+      else
+        tma_store_4d(map, slab, 0, 0, h, tc.m0);
+      bulk_commit();
+    }
+  }
+}
+
+// Residual add + row L2 norm. Each warp owns 32 rows x 128 columns (its half): the accumulator goes
+// through a padded shared-memory transpose 32 columns at a time, so X and xn are read and written as
+// coalesced 128-byte row segments with all 32 rows' loads in flight before any store. Per-lane partial
+// sums of squares are combined with a 31-shuffle transpose-reduce (row `lane` ends in lane `lane`),
+// then the two halves of each row meet in shared memory.
+template <int BN, typename TIn>
+__device__ __forceinline__ void epi_resnorm(const GemmArgs& a, const TileCoord& tc, EpiCtx& e, int local_tile) {
   float* X = static_cast<float*>(a.out0);
   TIn* xn = static_cast<TIn*>(a.out1);
+  const int lane = e.lane;
+  const int row0 = tc.m0 + e.quarter * 32;
   const int nrows = min(32, a.M - row0);  // rows of this warp that exist (may be <= 0)
+  float* stage = e.scratch + e.ewarp * (32 * 33);
   float ps[32];
 #pragma unroll
   for (int r = 0; r < 32; ++r) ps[r] = 0.f;
 #pragma unroll 1
-  for (int c = 0; c < 8; ++c) {
+  for (int c = 0; c < BN / 64; ++c) {
+    const int col = e.hf * (BN / 2) + c * 32;
     float v[32];
-    tmem_ld32(taddr + c * 32, v);
+    tmem_ld32(e.taddr + col, v);
 #pragma unroll
     for (int i = 0; i < 32; ++i) stage[lane * 33 + i] = v[i];
     __syncwarp();
-    const int col = c * 32 + lane;
-    const float b = a.bias ? a.bias[col] : 0.f;
+    const float b = a.bias ? a.bias[col + lane] : 0.f;
+    float* xr = X + ((size_t)row0 * 256 + col + lane);  // row r of this warp at xr[r * 256]
     float x[32];
 #pragma unroll
-    for (int r = 0; r < 32; ++r) x[r] = r < nrows ? X[(size_t)(row0 + r) * 256 + col] : 0.f;
+    for (int r = 0; r < 32; ++r) x[r] = r < nrows ? xr[r * 256] : 0.f;
 #pragma unroll
     for (int r = 0; r < 32; ++r) {
       x[r] += stage[r * 33 + lane] + b;
@@ -190,11 +312,9 @@ __device__ __forceinline__ void epi_resnorm(const GemmArgs& a, uint32_t taddr, i
     }
 #pragma unroll
     for (int r = 0; r < 32; ++r)
-      if (r < nrows) X[(size_t)(row0 + r) * 256 + col] = x[r];
+      if (r < nrows) xr[r * 256] = x[r];
     __syncwarp();
   }
-  // transpose-reduce: after the step with offset o, ps[i] (i < o) holds the pair-sum of the row
-  // selected by the lane bits above o
 #pragma unroll
   for (int o = 16; o >= 1; o >>= 1) {
     const bool upper = (lane & o) != 0;
@@ -205,70 +325,85 @@ __device__ __forceinline__ void epi_resnorm(const GemmArgs& a, uint32_t taddr, i
       ps[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
     }
   }
-  const float inv = 1.0f / fmaxf(sqrtf(ps[0]), a.eps);  // for row `lane`
+  float* rs = e.scratch + kEpiWarps * 32 * 33 + (local_tile & 1) * 256;
+  rs[e.hf * 128 + e.quarter * 32 + lane] = ps[0];
+  named_bar(3, 32 * kEpiWarps);
+  const float tot = rs[e.quarter * 32 + lane] + rs[128 + e.quarter * 32 + lane];
+  const float inv = 1.0f / fmaxf(sqrtf(tot), a.eps);  // for row row0 + lane
 #pragma unroll 1
-  for (int c = 0; c < 8; ++c) {
-    const int col = c * 32 + lane;
+  for (int c = 0; c < BN / 64; ++c) {
+    const int col = e.hf * (BN / 2) + c * 32;
+    const float* xr = X + ((size_t)row0 * 256 + col + lane);
+    TIn* nr = xn + ((size_t)row0 * 256 + col + lane);
     float x[32];
 #pragma unroll
-    for (int r = 0; r < 32; ++r) x[r] = r < nrows ? X[(size_t)(row0 + r) * 256 + col] : 0.f;
+    for (int r = 0; r < 32; ++r) x[r] = r < nrows ? xr[r * 256] : 0.f;
 #pragma unroll
     for (int r = 0; r < 32; ++r) {
       const float iv = __shfl_sync(0xffffffffu, inv, r);
-      if (r < nrows) xn[(size_t)(row0 + r) * 256 + col] = OperandType<TIn>::from_float(x[r] * iv);
+      if (r < nrows) nr[r * 256] = OperandType<TIn>::from_float(x[r] * iv);
     }
   }
 }
 
+// GELU (dense) or tanh (grouped mask layer 1) on acc + bias, stored as 16-bit through TMA.
 template <int BN, typename TIn>
-__device__ __forceinline__ void epi_act(const GemmArgs& a, const TileCoord& tc, uint32_t taddr, int m, bool valid,
+__device__ __forceinline__ void epi_act(const GemmArgs& a, const TileCoord& tc, EpiCtx& e, const CUtensorMap* mo,
                                         bool tanh_act) {
-  TIn* out;
-  const float* bias;
-  if (a.n_groups == 0) {
-    out = static_cast<TIn*>(a.out0) + (size_t)m * a.ld_out + tc.n0;
-    bias = a.bias + tc.n0;
-  } else {  // mask layer 1: Hm[group][row][col]
-    out = static_cast<TIn*>(a.out0) + ((size_t)tc.group * a.M + m) * a.ld_out + tc.n0;
-    bias = a.bias + tc.b_row;
-  }
+  const float* bias = a.bias + tc.b_row;
 #pragma unroll 1
-  for (int c = 0; c < BN / 32; ++c) {
-    float v[32];
-    tmem_ld32(taddr + c * 32, v);
-    if (valid) {
-      const float4* bp = reinterpret_cast<const float4*>(bias + c * 32);
+  for (int hh = 0; hh < 2; ++hh) {
+    const int col = e.hf * (BN / 2) + hh * 64;
+    uint8_t* slab = slab_acquire(e);
+    float v0[32], v1[32];
+    tmem_ld32(e.taddr + col, v0);
+    tmem_ld32(e.taddr + col + 32, v1);
+    const float4* bp = reinterpret_cast<const float4*>(bias + col);
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const float4 bb = bp[q];
-        v[4 * q] += bb.x; v[4 * q + 1] += bb.y; v[4 * q + 2] += bb.z; v[4 * q + 3] += bb.w;
-      }
+    for (int q = 0; q < 8; ++q) {
+      const float4 b0 = bp[q], b1 = bp[8 + q];
+      v0[4 * q] += b0.x; v0[4 * q + 1] += b0.y; v0[4 * q + 2] += b0.z; v0[4 * q + 3] += b0.w;
+      v1[4 * q] += b1.x; v1[4 * q + 1] += b1.y; v1[4 * q + 2] += b1.z; v1[4 * q + 3] += b1.w;
+    }
 #pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] = tanh_act ? tanhf(v[i]) : gelu_erf(v[i]);
-      store32<TIn>(out + c * 32, v);
+    for (int i = 0; i < 32; ++i) {
+      v0[i] = tanh_act ? tanhf(v0[i]) : gelu_erf(v0[i]);
+      v1[i] = tanh_act ? tanhf(v1[i]) : gelu_erf(v1[i]);
+    }
+    stage_slab_row<TIn>(slab, e.row, v0, v1);
+    slab_release(e);
+    if (e.leader) {
+      if (a.n_groups > 0)
+        tma_store_3d(mo, slab, tc.n0 + col, tc.m0, tc.group);
+      else
+        tma_store_2d(mo, slab, tc.n0 + col, tc.m0);
+      bulk_commit();
     }
   }
 }
 
 template <int BN>
-__device__ __forceinline__ void epi_glu(const GemmArgs& a, const TileCoord& tc, uint32_t taddr, int m, bool valid) {
+__device__ __forceinline__ void epi_glu(const GemmArgs& a, const TileCoord& tc, EpiCtx& e) {
   const int g = tc.group;
   const int din = a.g_ncols[g] >> 1;
+  const int m = tc.m0 + e.row;
+  const bool valid = m < a.M;
   float* out = static_cast<float*>(a.out0) + (size_t)m * a.ld_out + a.g_outoff[g];
   const float* bias = a.bias + tc.b_row;
 #pragma unroll 1
-  for (int c = 0; c < BN / 32; ++c) {
-    if (c * 32 >= tc.n_mma) break;  // uniform over the CTA
+  for (int c = 0; c < BN / 64; ++c) {
+    const int col = e.hf * (BN / 2) + c * 32;
+    if (col >= tc.n_mma) break;  // uniform over the warp
     float v[32];
-    tmem_ld32(taddr + c * 32, v);
+    tmem_ld32(e.taddr + col, v);
     if (valid) {
-      const int col0 = tc.n0 + c * 32;  // interleaved column: (a, g) pairs
+      const int col0 = tc.n0 + col;  // interleaved column: (a, g) pairs
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
         const int cc = (col0 >> 1) + i;
         if (cc < din) {
-          const float av = v[2 * i] + bias[c * 32 + 2 * i];
-          const float gv = v[2 * i + 1] + bias[c * 32 + 2 * i + 1];
+          const float av = v[2 * i] + bias[col + 2 * i];
+          const float gv = v[2 * i + 1] + bias[col + 2 * i + 1];
           out[cc] = av * sigmoidf_(gv);
         }
       }
@@ -282,16 +417,18 @@ struct GemmSmem {
   static constexpr int kABytes = kGemmBM * kGemmBK * 2;  // 16 KB
   static constexpr int kBBytes = BN * kGemmBK * 2;       // 32 KB at BN = 256
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStageOffset = STAGES * kStageBytes;        // epilogue transpose buffers
-  static constexpr int kEpiStageBytes = 4 * 32 * 33 * 4;           // 4 warps x [32][33] fp32
-  static constexpr int kBarOffset = kStageOffset + kEpiStageBytes;
+  static constexpr int kOutOffset = STAGES * kStageBytes;  // 4 staging slabs / residual-norm scratch
+  static constexpr int kOutBytes = 4 * kSlabBytes;
+  static_assert(kEpiWarps * 32 * 33 * 4 + 2 * 256 * 4 <= kOutBytes, "residual-norm scratch must fit");
+  static constexpr int kBarOffset = kOutOffset + kOutBytes;
   static constexpr int kBytes = kBarOffset + 256 + 1024;  // + barriers + alignment slack
 };
 
 template <int BN, int STAGES, int EPI, typename TIn>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                const __grid_constant__ GemmArgs args) {
+                const __grid_constant__ CUtensorMap map_o0, const __grid_constant__ CUtensorMap map_o1,
+                const __grid_constant__ CUtensorMap map_o2, const __grid_constant__ GemmArgs args) {
   using S = GemmSmem<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -305,6 +442,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const int a_dims = args.a_mode == A_ROWS ? 2 : args.a_mode == A_TIME_SEQ ? 4 : 3;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -313,7 +451,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 128);
+      mbar_init(&acc_empty[b], 32 * kEpiWarps);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -350,12 +488,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           uint8_t* sb = sa + S::kABytes;
           mbar_arrive_expect_tx(&full[stage], S::kStageBytes);
           const int kx = kb * kGemmBK;
-          if (args.a_mode == 0)
-            tma_load_2d(sa, &map_a, &full[stage], kx, tc.m0);
-          else if (args.a_mode == 1)
-            tma_load_3d(sa, &map_a, &full[stage], kx, tc.group, tc.m0);
+          if (a_dims == 2)
+            tma_load_2d(sa, &map_a, &full[stage], kx, tc.a1);
+          else if (a_dims == 3)
+            tma_load_3d(sa, &map_a, &full[stage], kx, tc.a1, tc.a2);
           else
-            tma_load_3d(sa, &map_a, &full[stage], kx, tc.m0, tc.group);
+            tma_load_4d(sa, &map_a, &full[stage], kx, tc.a1, tc.a2, tc.a3);
           tma_load_2d(sb, &map_b, &full[stage], kx, tc.b_row);
           ++issued;
           if (++stage == STAGES) {
@@ -420,35 +558,42 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   } else {
-    // ------------------------------------------------------------------ epilogue (warps 2-5)
-    const int quarter = warp & 3;
-    const int row = quarter * 32 + lane;
+    // ------------------------------------------------------------------ epilogue (warps 2-9)
+    EpiCtx e;
+    e.lane = lane;
+    e.quarter = warp & 3;
+    e.ewarp = warp - 2;
+    e.hf = e.ewarp >> 2;
+    e.row = e.quarter * 32 + lane;
+    e.leader = (e.ewarp & 3) == 0 && lane == 0;
+    e.slabs = smem + S::kOutOffset;
+    e.scratch = reinterpret_cast<float*>(smem + S::kOutOffset);
+    e.slot = 0;
     int local = 0;
     for (int tile = blockIdx.x; tile < args.num_tiles; tile += gridDim.x, ++local) {
       const TileCoord tc = gemm_decode<BN>(args, tile);
       const int buf = local & 1;
       const uint32_t use = (uint32_t)(local >> 1);
-      if (!mbar_wait_warp(&acc_full[buf], use & 1, args.err, kErrWaitEpilogue, abort_flag)) break;
+      // every epilogue warp takes the same decision, so no warp is left waiting at a named barrier
+      const bool ok = mbar_wait_warp(&acc_full[buf], use & 1, args.err, kErrWaitEpilogue, abort_flag);
+      if (!named_bar_and(4, 32 * kEpiWarps, ok)) break;
       tc_fence_after();
-      const uint32_t taddr = tmem_base + (uint32_t)(buf * BN) + ((uint32_t)(quarter * 32) << 16);
-      const int m = tc.m0 + row;
-      const bool valid = m < args.M;
+      e.taddr = tmem_base + (uint32_t)(buf * BN) + ((uint32_t)(e.quarter * 32) << 16);
       if constexpr (EPI == EPI_QKV) {
-        epi_qkv<BN, TIn>(args, tc, taddr, m, valid);
+        epi_qkv<BN, TIn>(args, tc, e, &map_o0, &map_o1, &map_o2);
       } else if constexpr (EPI == EPI_RESNORM) {
-        float* stage = reinterpret_cast<float*>(smem + S::kStageOffset) + quarter * 32 * 33;
-        epi_resnorm<BN, TIn>(args, tmem_base + (uint32_t)(buf * BN) + ((uint32_t)(quarter * 32) << 16),
-                             tc.m0 + quarter * 32, lane, stage);
+        epi_resnorm<BN, TIn>(args, tc, e, local);
       } else if constexpr (EPI == EPI_GELU) {
-        epi_act<BN, TIn>(args, tc, taddr, m, valid, false);
+        epi_act<BN, TIn>(args, tc, e, &map_o0, false);
       } else if constexpr (EPI == EPI_MASK_TANH) {
-        epi_act<BN, TIn>(args, tc, taddr, m, valid, true);
+        epi_act<BN, TIn>(args, tc, e, &map_o0, true);
       } else {
-        epi_glu<BN>(args, tc, taddr, m, valid);
+        epi_glu<BN>(args, tc, e);
       }
       tc_fence_before();
       mbar_arrive(&acc_empty[buf]);
     }
+    if (e.leader) bulk_wait<0>();  // this half's output stores have completed
   }
 
   tc_fence_before();

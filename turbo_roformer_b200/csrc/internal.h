@@ -23,9 +23,10 @@ void launch_add_rmsnorm(float* X, const float* Y, void* out, int out_f32, int64_
 void launch_chunk_ola(const float* chunks, int64_t clen, const int64_t* d_starts, int n_chunks, const float* w,
                       int64_t n, float* out, cudaStream_t st);
 
-// tc.cu (tensor-core kernels). epi: EpiKind; precision: 0 fp16, 1 bf16. Return cudaError_t of the launch.
+// tc.cu (tensor-core kernels). epi: EpiKind; precision: 0 fp16, 1 bf16; map_out: 3 output tensor maps
+// (unused ones may hold anything). Return cudaError_t of the launch.
 cudaError_t launch_gemm(int epi, int precision, const CUtensorMap& map_a, const CUtensorMap& map_b,
-                        const GemmArgs& args, int num_sms, cudaStream_t st);
+                        const CUtensorMap* map_out, const GemmArgs& args, int num_sms, cudaStream_t st);
 cudaError_t launch_attention(int precision, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                              const AttnArgs& args, cudaStream_t st);
 

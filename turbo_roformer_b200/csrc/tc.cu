@@ -1,4 +1,6 @@
 // Instantiation and launch of the tensor-core kernels (tcgen05 GEMM with fused epilogues, attention).
+#include <atomic>
+
 #include "attention.cuh"
 #include "gemm.cuh"
 #include "internal.h"
@@ -7,32 +9,46 @@ namespace trc {
 
 namespace {
 
+// The dynamic shared-memory opt-in is per function and per device: set it once for each pair.
+// `done` must be a distinct object per kernel instantiation (callers pass a function-local static).
+template <typename Kern>
+cudaError_t allow_smem(Kern kern, int bytes, std::atomic<unsigned long long>& done) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (done.load(std::memory_order_relaxed) & bit) return cudaSuccess;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done.fetch_or(bit);
+  return e;
+}
+
 constexpr int kBN = 256;
-constexpr int kStages = 4;
+constexpr int kStages = 3;
 
 template <int EPI, typename T>
-cudaError_t launch_gemm_t(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& args, int num_sms,
-                          cudaStream_t st) {
+cudaError_t launch_gemm_t(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap* mo, const GemmArgs& args,
+                          int num_sms, cudaStream_t st) {
   using S = GemmSmem<kBN, kStages>;
   auto kern = gemm_kernel<kBN, kStages, EPI, T>;
-  // the attribute is per function and per device: set it on every launch (a cheap host call)
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBytes);
+  static std::atomic<unsigned long long> done{0};  // one per <EPI, T> instantiation
+  cudaError_t e = allow_smem(kern, S::kBytes, done);
   if (e != cudaSuccess) return e;
   if (args.num_tiles <= 0) return cudaSuccess;
   const int grid = args.num_tiles < num_sms ? args.num_tiles : num_sms;
-  kern<<<grid, kGemmThreads, S::kBytes, st>>>(ma, mb, args);
+  kern<<<grid, kGemmThreads, S::kBytes, st>>>(ma, mb, mo[0], mo[1], mo[2], args);
   return cudaGetLastError();
 }
 
 template <typename T>
-cudaError_t launch_gemm_p(int epi, const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& args, int num_sms,
-                          cudaStream_t st) {
+cudaError_t launch_gemm_p(int epi, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap* mo,
+                          const GemmArgs& args, int num_sms, cudaStream_t st) {
   switch (epi) {
-    case EPI_QKV: return launch_gemm_t<EPI_QKV, T>(ma, mb, args, num_sms, st);
-    case EPI_RESNORM: return launch_gemm_t<EPI_RESNORM, T>(ma, mb, args, num_sms, st);
-    case EPI_GELU: return launch_gemm_t<EPI_GELU, T>(ma, mb, args, num_sms, st);
-    case EPI_MASK_TANH: return launch_gemm_t<EPI_MASK_TANH, T>(ma, mb, args, num_sms, st);
-    case EPI_MASK_GLU: return launch_gemm_t<EPI_MASK_GLU, T>(ma, mb, args, num_sms, st);
+    case EPI_QKV: return launch_gemm_t<EPI_QKV, T>(ma, mb, mo, args, num_sms, st);
+    case EPI_RESNORM: return launch_gemm_t<EPI_RESNORM, T>(ma, mb, mo, args, num_sms, st);
+    case EPI_GELU: return launch_gemm_t<EPI_GELU, T>(ma, mb, mo, args, num_sms, st);
+    case EPI_MASK_TANH: return launch_gemm_t<EPI_MASK_TANH, T>(ma, mb, mo, args, num_sms, st);
+    case EPI_MASK_GLU: return launch_gemm_t<EPI_MASK_GLU, T>(ma, mb, mo, args, num_sms, st);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -41,7 +57,8 @@ template <typename T>
 cudaError_t launch_attention_t(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                                const AttnArgs& args, cudaStream_t st) {
   auto kern = attention_kernel<T>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnSmem::kBytes);
+  static std::atomic<unsigned long long> done{0};  // one per <T> instantiation
+  cudaError_t e = allow_smem(kern, AttnSmem::kBytes, done);
   if (e != cudaSuccess) return e;
   if (args.num_tiles <= 0) return cudaSuccess;
   kern<<<args.num_tiles, kAttnThreads, AttnSmem::kBytes, st>>>(mq, mk, mv, args);
@@ -50,10 +67,10 @@ cudaError_t launch_attention_t(const CUtensorMap& mq, const CUtensorMap& mk, con
 
 }  // namespace
 
-cudaError_t launch_gemm(int epi, int precision, const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& args,
-                        int num_sms, cudaStream_t st) {
-  return precision == 0 ? launch_gemm_p<__half>(epi, ma, mb, args, num_sms, st)
-                        : launch_gemm_p<__nv_bfloat16>(epi, ma, mb, args, num_sms, st);
+cudaError_t launch_gemm(int epi, int precision, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap* mo,
+                        const GemmArgs& args, int num_sms, cudaStream_t st) {
+  return precision == 0 ? launch_gemm_p<__half>(epi, ma, mb, mo, args, num_sms, st)
+                        : launch_gemm_p<__nv_bfloat16>(epi, ma, mb, mo, args, num_sms, st);
 }
 
 cudaError_t launch_attention(int precision, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
