@@ -244,7 +244,23 @@ struct Section {
       cudaEventRecord(e1, st);
       h->ev_pending.push_back({name, {e0, e1}});
       h->section[name].second += launches;
+      if (h->ev_pending.size() >= 512) harvest(h);
     }
+  }
+  // Fold finished event pairs (oldest first, non-blocking) into the totals and recycle the events, so
+  // long timed runs never create events on the launch path.
+  static void harvest(trc_handle* h) {
+    size_t k = 0;
+    for (; k < h->ev_pending.size(); ++k) {
+      auto& p = h->ev_pending[k];
+      if (cudaEventQuery(p.second.second) != cudaSuccess) break;
+      float ms = 0.f;
+      if (cudaEventElapsedTime(&ms, p.second.first, p.second.second) == cudaSuccess) h->section[p.first].first += ms;
+      h->ev_pool.push_back(p.second.first);
+      h->ev_pool.push_back(p.second.second);
+    }
+    cudaGetLastError();  // a not-ready query leaves cudaErrorNotReady behind
+    h->ev_pending.erase(h->ev_pending.begin(), h->ev_pending.begin() + k);
   }
 };
 
@@ -434,17 +450,18 @@ int run_attention(trc_handle* h, int mode, const void* Q, const void* K, const v
   if (mode == 0) {
     a.L = T;
     a.BH = B * F * 8;
-    a.q_tiles = (T + 127) / 128;
-    a.n_kv = a.q_tiles;
-    a.num_tiles = a.BH * a.q_tiles;
+    const int q_tiles = (T + 127) / 128;
+    a.q_pairs = (q_tiles + 1) / 2;
+    a.n_kv = q_tiles;
+    a.num_items = a.BH * a.q_pairs;
     box[0] = 64; box[1] = 128; box[2] = 1;
   } else {
     if (F > 64) return fail(TRC_E_INVALID, "freq attention supports at most 64 bands");
     a.L = F;
     a.BH = B * T * 8;
-    a.q_tiles = 1;
+    a.q_pairs = 1;
     a.n_kv = 1;
-    a.num_tiles = (a.BH + 1) / 2;
+    a.num_items = (a.BH + 3) / 4;
     box[0] = 64; box[1] = 64; box[2] = 2;
   }
   dims[0] = 64;
@@ -457,7 +474,7 @@ int run_attention(trc_handle* h, int mode, const void* Q, const void* K, const v
   if ((rc = make_map_cached(h, &mq, Q, 3, dims, strides, box)) || (rc = make_map_cached(h, &mk, K, 3, dims, strides, box)) ||
       (rc = make_map_cached(h, &mv, V, 3, dims, strides, box)))
     return rc;
-  return check_launch(trc::launch_attention(h->prec, mq, mk, mv, a, st), "attention");
+  return check_launch(trc::launch_attention(h->prec, mq, mk, mv, a, h->num_sms, st), "attention");
 }
 
 int run_res_norm(trc_handle* h, int layer, int which, const void* A, float* X, void* xn, int64_t rows,

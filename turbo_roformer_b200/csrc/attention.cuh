@@ -3,16 +3,27 @@
 // Replaces the reference's AVX-512 `attention` kernel (LoggeL/turbo-roformer
 // src/turbo_roformer/csrc/kernels.cpp:255-388): per (sequence, head) S = Q K^T (scale folded into W_q),
 // softmax over the keys, O = P V, then x sigmoid gate, head merge and scatter back to token order.
-// The reference keeps whole score rows (two passes); here one CTA owns 128 query rows and streams
-// 128-key tiles: S and the PV partial product live in TMEM, unnormalised P (16-bit) is staged in
-// shared memory in the 128-byte-swizzled K-major layout the tensor core reads.
+// The reference keeps whole score rows (two passes); here a CTA owns two 128-row query tiles (A, B)
+// and streams 128-key tiles:
+//   * S = Q K^T (both operands in shared memory) lands in TMEM; the softmax warpgroup of the tile reads
+//     it, writes unnormalised 16-bit P back into the same TMEM columns, and the tensor core computes
+//     O += P V with P read straight from TMEM (no shared-memory round trip for P).
+//   * O accumulates in TMEM. The running row maximum is only raised when a tile's maximum exceeds it
+//     by more than 2^8 (then O and the row sum are rescaled in place); P <= 2^8 keeps 16-bit P exact
+//     enough and the final O / l is the exact softmax average.
+//   * The MMA issuer ping-pongs between the tiles (PV_A, S_A next, PV_B, S_B next) so one tile's
+//     softmax overlaps the other tile's matrix products.
+//   * Persistent CTAs walk the work items; Q is double buffered so the next item's first products
+//     start while the current item's epilogue runs.
 //
 // Layout: Q, K, V are [BH, L, 64] 16-bit, row-major, unpadded; the 3-D TMA maps zero-fill rows >= L.
-//   time mode (mode 0): sequences = (batch, band, head), L = T frames, one sequence per CTA tile.
-//   freq mode (mode 1): sequences = (batch, frame, head), L = bands <= 64, two sequences per 128-row
-//                       tile with a block-diagonal mask.
-// Roles (192 threads): warp 0 TMA, warp 1 MMA issuer + TMEM owner, warps 2-5 softmax + epilogue
-// (thread = query row).
+//   time mode (mode 0): sequences = (batch, band, head), L = T frames; an item = one sequence and two
+//                       consecutive 128-row query tiles; every key tile serves both query tiles.
+//   freq mode (mode 1): sequences = (batch, frame, head), L = bands <= 64; a query tile holds two
+//                       sequences (block-diagonal mask), an item = four sequences, each tile has its own
+//                       single key tile.
+// Roles (320 threads): warp 0 TMA, warp 1 MMA issuer + TMEM owner, warps 2-5 softmax + epilogue of
+// tile A, warps 6-9 of tile B (thread = query row).
 #pragma once
 
 #include "gemm.cuh"  // store32
@@ -20,17 +31,17 @@
 
 namespace trc {
 
-constexpr int kAttnThreads = 192;
+constexpr int kAttnThreads = 320;
 constexpr int kAttnKvStages = 3;
 
 struct AttnArgs {
-  int num_tiles;
-  int q_tiles;  // query tiles per sequence (time) ; 1 (freq)
-  int n_kv;     // key tiles per sequence (time) ; 1 (freq)
-  int L;        // valid length of every sequence
-  int BH;       // number of sequences
-  int mode;     // 0 time, 1 freq
-  int T, F;     // frames, bands (per batch item)
+  int num_items;  // work items
+  int q_pairs;    // time: query-tile pairs per sequence
+  int n_kv;       // time: key tiles per sequence
+  int L;          // valid length of every sequence
+  int BH;         // number of sequences
+  int mode;       // 0 time, 1 freq
+  int T, F;       // frames, bands (per batch item)
   const float* G;  // gates [tokens][8]
   void* O;         // [tokens][512] 16-bit
   int* err;
@@ -38,13 +49,16 @@ struct AttnArgs {
 
 struct AttnSmem {
   static constexpr int kTile = 128 * 64 * 2;  // 16 KB: 128 rows x 64 dims
-  static constexpr int kQ = 0;
-  static constexpr int kK = kQ + kTile;
-  static constexpr int kV = kK + kAttnKvStages * kTile;
-  static constexpr int kP = kV + kAttnKvStages * kTile;  // 2 swizzle atoms along keys: 32 KB
-  static constexpr int kBar = kP + 2 * kTile;
-  static constexpr int kBytes = kBar + 256 + 1024;
+  static constexpr int kQ = 0;                 // [2 buffers][2 tiles]
+  static constexpr int kKV = kQ + 4 * kTile;   // [stages][K, V]
+  static constexpr int kBar = kKV + 2 * kAttnKvStages * kTile;
+  static constexpr int kBytes = kBar + 512 + 1024;
 };
+
+// TMEM columns: S_A [0,128), S_B [128,256) (P aliases their first 64 columns), O_A [256,320), O_B [320,384)
+__device__ __forceinline__ uint32_t tmem_col_s(int x) { return (uint32_t)x * 128u; }
+__device__ __forceinline__ uint32_t tmem_col_o(int x) { return 256u + (uint32_t)x * 64u; }
+constexpr float kRescaleThreshold = 8.0f;  // log2 units: P stays <= 2^8
 
 template <typename TIn>
 __global__ void __launch_bounds__(kAttnThreads, 1)
@@ -54,47 +68,37 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::kBar);
-  uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;
-  uint64_t* v_full = k_full + kAttnKvStages;
-  uint64_t* kv_empty = v_full + kAttnKvStages;
-  uint64_t* s_full = kv_empty + kAttnKvStages;  // [2]
-  uint64_t* s_empty = s_full + 2;               // [2]
-  uint64_t* p_full = s_empty + 2;
-  uint64_t* pv_full = p_full + 1;
-  uint64_t* pv_empty = pv_full + 1;
-  uint64_t* drain = pv_empty + 1;
+  uint64_t* q_full = bars;                   // [2] per Q buffer
+  uint64_t* q_empty = q_full + 2;            // [2]
+  uint64_t* kv_full = q_empty + 2;           // [stages]
+  uint64_t* kv_empty = kv_full + kAttnKvStages;
+  uint64_t* s_full = kv_empty + kAttnKvStages;  // [2] per query tile
+  uint64_t* p_full = s_full + 2;                // [2]
+  uint64_t* o_full = p_full + 2;                // [2]
+  uint64_t* o_free = o_full + 2;                // [2]
+  uint64_t* drain = o_free + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int tile = blockIdx.x;
   const bool freq = args.mode == 1;
-  int bh0, q0;
-  if (freq) {
-    bh0 = 2 * tile;
-    q0 = 0;
-  } else {
-    bh0 = tile / args.q_tiles;
-    q0 = (tile - bh0 * args.q_tiles) * 128;
-  }
-  const int n_kv = args.n_kv;
+  const int nsteps = freq ? 1 : args.n_kv;       // key tiles per query tile and item
+  const int kv_per_item = freq ? 2 : args.n_kv;  // key/value loads per item
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&q_full[b], 1);
+      mbar_init(&q_empty[b], 1);
+      mbar_init(&s_full[b], 1);
+      mbar_init(&p_full[b], 128);
+      mbar_init(&o_full[b], 1);
+      mbar_init(&o_free[b], 128);
+    }
     for (int s = 0; s < kAttnKvStages; ++s) {
-      mbar_init(&k_full[s], 1);
-      mbar_init(&v_full[s], 1);
+      mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&s_full[b], 1);
-      mbar_init(&s_empty[b], 128);
-    }
-    mbar_init(p_full, 128);
-    mbar_init(pv_full, 1);
-    mbar_init(pv_empty, 128);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -105,7 +109,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     tma_prefetch_desc(&map_v);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 512);  // S0 [0,128), S1 [128,256), PV [256,320)
+    tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -116,214 +120,247 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      mbar_arrive_expect_tx(q_full, S::kTile);
-      tma_load_3d(smem + S::kQ, &map_q, q_full, 0, q0, bh0);
-      int issued = 0;
+      int kvc = 0, local = 0, q_issued = 0;
       bool ok = true;
-      for (int j = 0; j < n_kv; ++j) {
-        const int st = j % kAttnKvStages;
-        const uint32_t u = (uint32_t)(j / kAttnKvStages);
-        if (!mbar_wait(&kv_empty[st], (u & 1) ^ 1, args.err, kErrWaitProducer, abort_flag)) {
+      for (int item = blockIdx.x; item < args.num_items && ok; item += gridDim.x, ++local) {
+        int bh, q0;
+        if (freq) {
+          bh = 4 * item;
+          q0 = 0;
+        } else {
+          bh = item / args.q_pairs;
+          q0 = (item - bh * args.q_pairs) * 256;
+        }
+        const int qb = local & 1;
+        if (!mbar_wait(&q_empty[qb], ((uint32_t)(local >> 1) & 1) ^ 1, args.err, kErrWaitProducer, abort_flag)) {
           ok = false;
           break;
         }
-        mbar_arrive_expect_tx(&k_full[st], S::kTile);
-        tma_load_3d(smem + S::kK + st * S::kTile, &map_k, &k_full[st], 0, j * 128, bh0);
-        mbar_arrive_expect_tx(&v_full[st], S::kTile);
-        tma_load_3d(smem + S::kV + st * S::kTile, &map_v, &v_full[st], 0, j * 128, bh0);
-        ++issued;
-      }
-      {  // drain: wait (bounded) until every issued copy has landed before the CTA may exit
-        const uint64_t t0 = global_ns();
-        while (!mbar_try_wait(q_full, 0) && global_ns() - t0 < kWaitLimitNs) {
+        mbar_arrive_expect_tx(&q_full[qb], 2 * S::kTile);
+        uint8_t* qbuf = smem + S::kQ + qb * 2 * S::kTile;
+        if (freq) {
+          tma_load_3d(qbuf, &map_q, &q_full[qb], 0, 0, bh);
+          tma_load_3d(qbuf + S::kTile, &map_q, &q_full[qb], 0, 0, bh + 2);
+        } else {
+          tma_load_3d(qbuf, &map_q, &q_full[qb], 0, q0, bh);
+          tma_load_3d(qbuf + S::kTile, &map_q, &q_full[qb], 0, q0 + 128, bh);
         }
-        if (!ok) {
-          for (int j = max(0, issued - kAttnKvStages); j < issued; ++j) {
-            const int st = j % kAttnKvStages;
-            const uint32_t ph = (uint32_t)(j / kAttnKvStages) & 1;
-            const uint64_t t1 = global_ns();
-            while (!(mbar_try_wait(&k_full[st], ph) && mbar_try_wait(&v_full[st], ph)) &&
-                   global_ns() - t1 < kWaitLimitNs) {
-            }
+        ++q_issued;
+        for (int j = 0; j < kv_per_item; ++j) {
+          const int st = kvc % kAttnKvStages;
+          const uint32_t u = (uint32_t)(kvc / kAttnKvStages);
+          if (!mbar_wait(&kv_empty[st], (u & 1) ^ 1, args.err, kErrWaitProducer, abort_flag)) {
+            ok = false;
+            break;
           }
+          uint8_t* kb = smem + S::kKV + st * 2 * S::kTile;
+          mbar_arrive_expect_tx(&kv_full[st], 2 * S::kTile);
+          const int row = freq ? 0 : j * 128;
+          const int seq = freq ? bh + 2 * j : bh;
+          tma_load_3d(kb, &map_k, &kv_full[st], 0, row, seq);
+          tma_load_3d(kb + S::kTile, &map_v, &kv_full[st], 0, row, seq);
+          ++kvc;
         }
       }
+      // let the last issued copies land before the CTA may exit (they are consumed already unless an
+      // error aborted the pipeline); bounded like every wait
+      const uint64_t t0 = global_ns();
+      for (int k = max(0, kvc - kAttnKvStages); k < kvc; ++k)
+        while (!mbar_try_wait(&kv_full[k % kAttnKvStages], (uint32_t)(k / kAttnKvStages) & 1) &&
+               global_ns() - t0 < kWaitLimitNs) {
+        }
+      for (int k = max(0, q_issued - 2); k < q_issued; ++k)
+        while (!mbar_try_wait(&q_full[k & 1], (uint32_t)(k >> 1) & 1) && global_ns() - t0 < kWaitLimitNs) {
+        }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t idesc_qk = idesc_f16(128, 128, OperandType<TIn>::kFormat, 0, 0);
       const uint32_t idesc_pv = idesc_f16(128, 64, OperandType<TIn>::kFormat, 0, 1);  // V is MN-major
-      const uint32_t sq = smem_u32(smem + S::kQ);
-      const uint32_t sp = smem_u32(smem + S::kP);
-      bool ok = mbar_wait(q_full, 0, args.err, kErrWaitMma, abort_flag);
-      auto issue_pv = [&](int i) -> bool {
-        const int st = i % kAttnKvStages;
-        const uint32_t u = (uint32_t)(i / kAttnKvStages);
-        if (!mbar_wait(p_full, (uint32_t)i & 1, args.err, kErrWaitMma, abort_flag)) return false;
-        if (!mbar_wait(&v_full[st], u & 1, args.err, kErrWaitMma, abort_flag)) return false;
-        if (!mbar_wait(pv_empty, ((uint32_t)i & 1) ^ 1, args.err, kErrWaitMma, abort_flag)) return false;
-        tc_fence_after();
-        const uint32_t sv = smem_u32(smem + S::kV + st * S::kTile);
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {  // 16 keys per MMA
-          const uint64_t ad = sdesc_sw128(sp + (kk >> 2) * S::kTile + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = sdesc_sw128(sv + kk * 2048, 8192, 1024);
-          mma_f16_ss(tmem_base + 256, ad, bd, idesc_pv, kk > 0 ? 1u : 0u);
-        }
-        mma_commit(pv_full);
-        mma_commit(&kv_empty[st]);
-        return true;
+      int kvc = 0, local = 0;
+      int steps[2] = {0, 0};  // S tiles issued per query tile (s_full / p_full phase counters)
+      bool ok = true;
+      auto wait = [&](uint64_t* bar, uint32_t parity) {
+        if (ok && !mbar_wait(bar, parity, args.err, kErrWaitMma, abort_flag)) ok = false;
+        return ok;
       };
-      for (int j = 0; j < n_kv && ok; ++j) {
-        const int st = j % kAttnKvStages;
-        const uint32_t u = (uint32_t)(j / kAttnKvStages);
-        const int sb = j & 1;
-        if (!mbar_wait(&k_full[st], u & 1, args.err, kErrWaitMma, abort_flag) ||
-            !mbar_wait(&s_empty[sb], (((uint32_t)j >> 1) & 1) ^ 1, args.err, kErrWaitMma, abort_flag)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t sk = smem_u32(smem + S::kK + st * S::kTile);
+      for (int item = blockIdx.x; item < args.num_items && ok; item += gridDim.x, ++local) {
+        const int qb = local & 1;
+        if (!wait(&q_full[qb], (uint32_t)(local >> 1) & 1)) break;
+        const uint32_t sq = smem_u32(smem + S::kQ + qb * 2 * S::kTile);
+        auto kv_index = [&](int x, int j) { return freq ? kvc + x : kvc + j; };
+        auto issue_s = [&](int x, int j) {
+          const int idx = kv_index(x, j);
+          const int st = idx % kAttnKvStages;
+          if ((x == 0 || freq) && !wait(&kv_full[st], (uint32_t)(idx / kAttnKvStages) & 1)) return;
+          tc_fence_after();
+          const uint32_t sk = smem_u32(smem + S::kKV + st * 2 * S::kTile);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          const uint64_t ad = sdesc_sw128(sq + kk * 32, 16, 1024);
-          const uint64_t bd = sdesc_sw128(sk + kk * 32, 16, 1024);
-          mma_f16_ss(tmem_base + (uint32_t)(sb * 128), ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t ad = sdesc_sw128(sq + x * S::kTile + kk * 32, 16, 1024);
+            const uint64_t bd = sdesc_sw128(sk + kk * 32, 16, 1024);
+            mma_f16_ss(tmem_base + tmem_col_s(x), ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
+          }
+          mma_commit(&s_full[x]);
+          ++steps[x];
+        };
+        auto issue_pv = [&](int x, int j) {
+          if (!wait(&p_full[x], (uint32_t)(steps[x] - 1) & 1)) return;
+          if (j == 0 && local > 0 && !wait(&o_free[x], (uint32_t)(local - 1) & 1)) return;
+          tc_fence_after();
+          const int idx = kv_index(x, j);
+          const int st = idx % kAttnKvStages;
+          const uint32_t sv = smem_u32(smem + S::kKV + st * 2 * S::kTile + S::kTile);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {  // 16 keys per MMA: P columns kk*8.., V rows kk*16..
+            const uint64_t bd = sdesc_sw128(sv + kk * 2048, 8192, 1024);
+            mma_f16_ts(tmem_base + tmem_col_o(x), tmem_base + tmem_col_s(x) + kk * 8, bd, idesc_pv,
+                       (j > 0 || kk > 0) ? 1u : 0u);
+          }
+          if (j == nsteps - 1) mma_commit(&o_full[x]);
+          if (x == 1 || freq) mma_commit(&kv_empty[st]);  // last reader of this key/value stage
+        };
+        issue_s(0, 0);
+        issue_s(1, 0);
+        for (int j = 0; j < nsteps && ok; ++j) {
+          issue_pv(0, j);
+          if (j + 1 < nsteps) issue_s(0, j + 1);
+          issue_pv(1, j);
+          if (j + 1 < nsteps) issue_s(1, j + 1);
         }
-        mma_commit(&s_full[sb]);
-        if (j > 0 && !issue_pv(j - 1)) ok = false;
+        mma_commit(&q_empty[qb]);
+        kvc += kv_per_item;
       }
-      if (ok && n_kv > 0) issue_pv(n_kv - 1);
       mma_commit(drain);
       const uint64_t t0 = global_ns();
       while (!mbar_try_wait(drain, 0) && global_ns() - t0 < kWaitLimitNs) {
       }
     }
   } else {
-    // ------------------------------------------------------------------ softmax + epilogue (warps 2-5)
+    // ------------------------------------------------------------------ softmax + epilogue (warps 2-9)
+    const int x = (warp - 2) >> 2;  // query tile of this warpgroup
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;  // query row within the tile
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    const int seq = freq ? bh0 + (r >> 6) : bh0;
-    const int pos = freq ? (r & 63) : q0 + r;
-    const int my_block = r >> 6;  // freq: which of the two sequences
+    const uint32_t tS = tmem_base + lane_off + tmem_col_s(x);
+    const uint32_t tO = tmem_base + lane_off + tmem_col_o(x);
     const float kLog2e = 1.4426950408889634f;
-    float o[64];
-#pragma unroll
-    for (int i = 0; i < 64; ++i) o[i] = 0.f;
-    float m_run = -INFINITY, l_run = 0.f;
-    uint8_t* prow = smem + S::kP + r * 128;
-    bool ok = true;
-
-    for (int j = 0; j < n_kv; ++j) {
-      const int sb = j & 1;
-      if (!mbar_wait_warp(&s_full[sb], ((uint32_t)j >> 1) & 1, args.err, kErrWaitSoftmax, abort_flag)) {
-        ok = false;
-        break;
+    int step = 0, local = 0;
+    for (int item = blockIdx.x; item < args.num_items; item += gridDim.x, ++local) {
+      int seq, pos;
+      if (freq) {
+        seq = 4 * item + 2 * x + (r >> 6);
+        pos = r & 63;
+      } else {
+        const int bh = item / args.q_pairs;
+        seq = bh;
+        pos = (item - bh * args.q_pairs) * 256 + x * 128 + r;
       }
-      tc_fence_after();
-      const uint32_t s_addr = tmem_base + lane_off + (uint32_t)(sb * 128);
-      const int key0 = j * 128;
-      // pass 1: row maximum over the valid keys
-      float mx = -INFINITY;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        float v[32];
-        tmem_ld32(s_addr + c * 32, v);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int kc = c * 32 + i;
-          const bool kv = freq ? ((kc >> 6) == my_block && (kc & 63) < args.L) : (key0 + kc < args.L);
-          if (kv) mx = fmaxf(mx, v[i]);
-        }
-      }
-      const float m_new = fmaxf(m_run, mx * kLog2e);
-      // fold in the previous tile's P V (computed relative to m_run)
-      if (j > 0) {
-        if (!mbar_wait_warp(pv_full, (uint32_t)(j - 1) & 1, args.err, kErrWaitSoftmax, abort_flag)) {
+      const int my_block = r >> 6;
+      float m_run = -INFINITY, l_run = 0.f;
+      bool ok = true;
+      for (int j = 0; j < nsteps; ++j, ++step) {
+        if (!mbar_wait_warp(&s_full[x], (uint32_t)step & 1, args.err, kErrWaitSoftmax, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        float v[32];
-        tmem_ld32(tmem_base + lane_off + 256, v);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) o[i] += v[i];
-        tmem_ld32(tmem_base + lane_off + 256 + 32, v);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) o[32 + i] += v[i];
-        tc_fence_before();
-        mbar_arrive(pv_empty);
-      }
-      const float alpha = ex2_approx(m_run - m_new);  // 0 on the first tile (m_run = -inf)
-#pragma unroll
-      for (int i = 0; i < 64; ++i) o[i] *= alpha;
-      l_run *= alpha;
-      m_run = m_new;
-      // pass 2: P = 2^(s log2e - m), 16-bit, into the swizzled K-major P tile
+        const int key0 = j * 128;
+        const int kmax = freq ? 128 : min(128, args.L - key0);  // keys of this tile that exist
+        // pass 1: row maximum over the valid keys
+        float mx = -INFINITY;
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        float v[32];
-        tmem_ld32(s_addr + c * 32, v);
-        uint32_t packed[16];
+        for (int c = 0; c < 4; ++c) {
+          float v[32];
+          tmem_ld32(tS + c * 32, v);
+          if (freq) {
 #pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          float p2[2];
+            for (int i = 0; i < 32; ++i) {
+              const int kc = c * 32 + i;
+              if ((kc >> 6) == my_block && (kc & 63) < args.L) mx = fmaxf(mx, v[i]);
+            }
+          } else if (c * 32 + 32 <= kmax) {
 #pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int kc = c * 32 + i + e;
-            const bool kv = freq ? ((kc >> 6) == my_block && (kc & 63) < args.L) : (key0 + kc < args.L);
-            p2[e] = kv ? ex2_approx(fmaf(v[i + e], kLog2e, -m_run)) : 0.f;
-            l_run += p2[e];
+            for (int i = 0; i < 32; ++i) mx = fmaxf(mx, v[i]);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (c * 32 + i < kmax) mx = fmaxf(mx, v[i]);
           }
-          packed[i >> 1] = OperandType<TIn>::pack2(p2[0], p2[1]);
         }
+        const float m_tile = mx * kLog2e;
+        if (j == 0) {
+          m_run = m_tile;
+        } else {
+          const bool need = m_tile > m_run + kRescaleThreshold;
+          if (__any_sync(0xffffffffu, need)) {  // rescale O and l in place (O holds the steps < j)
+            const float alpha = need ? ex2_approx(m_run - m_tile) : 1.0f;
+            if (need) m_run = m_tile;
+            l_run *= alpha;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int chunk = c * 4 + q;  // 16-byte chunk (8 keys) within the 256-byte row
-          const int atom = chunk >> 3, cc = chunk & 7;
-          uint4* dst = reinterpret_cast<uint4*>(prow + atom * S::kTile + ((cc ^ (r & 7)) << 4));
-          *dst = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+            for (int h = 0; h < 2; ++h) {
+              float o[32];
+              tmem_ld32(tO + h * 32, o);
+#pragma unroll
+              for (int i = 0; i < 32; ++i) o[i] *= alpha;
+              tmem_st32(tO + h * 32, o);
+            }
+          }
         }
+        // pass 2: P = 2^(s log2e - m_run) as 16-bit pairs into the first 64 columns of S
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          float v[32];
+          tmem_ld32(tS + c * 32, v);
+          uint32_t packed[16];
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            float p2[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int kc = c * 32 + i + e;
+              const bool kv = freq ? ((kc >> 6) == my_block && (kc & 63) < args.L) : (kc < kmax);
+              p2[e] = kv ? ex2_approx(fmaf(v[i + e], kLog2e, -m_run)) : 0.f;
+              l_run += p2[e];
+            }
+            packed[i >> 1] = OperandType<TIn>::pack2(p2[0], p2[1]);
+          }
+          tmem_st16(tS + c * 16, packed);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&p_full[x]);
       }
+      if (!ok) break;
+      // epilogue: out = O / l * gate -> O[token][h*64 + d]
+      if (!mbar_wait_warp(&o_full[x], (uint32_t)local & 1, args.err, kErrWaitSoftmax, abort_flag)) break;
+      tc_fence_after();
+      float o0[32], o1[32];
+      tmem_ld32(tO, o0);
+      tmem_ld32(tO + 32, o1);
       tc_fence_before();
-      mbar_arrive(&s_empty[sb]);
-      fence_async_smem();
-      mbar_arrive(p_full);
-    }
-    if (ok && n_kv > 0) {
-      if (mbar_wait_warp(pv_full, (uint32_t)(n_kv - 1) & 1, args.err, kErrWaitSoftmax, abort_flag)) {
-        tc_fence_after();
-        float v[32];
-        tmem_ld32(tmem_base + lane_off + 256, v);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) o[i] += v[i];
-        tmem_ld32(tmem_base + lane_off + 256 + 32, v);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) o[32 + i] += v[i];
-        // epilogue: out = o / l * gate -> O[token][h*64 + d]
-        const bool valid = pos < args.L && seq < args.BH;
-        if (valid) {
-          const int h = seq & 7;
-          const int grp = seq >> 3;
-          long token;
-          if (!freq) {  // grp = b*F + f, pos = t
-            const int b = grp / args.F, f = grp - b * args.F;
-            token = ((long)b * args.T + pos) * args.F + f;
-          } else {  // grp = b*T + t, pos = f
-            token = (long)grp * args.F + pos;
-          }
-          const float scale = args.G[token * 8 + h] / l_run;
-          TIn* dst = static_cast<TIn*>(args.O) + token * 512 + h * 64;
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = o[i] * scale;
-          store32<TIn>(dst, v);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = o[32 + i] * scale;
-          store32<TIn>(dst + 32, v);
+      mbar_arrive(&o_free[x]);
+      const bool valid = pos < args.L && seq < args.BH;
+      if (valid) {
+        const int h = seq & 7;
+        const int grp = seq >> 3;
+        long token;
+        if (!freq) {  // grp = b*F + f, pos = t
+          const int b = grp / args.F, f = grp - b * args.F;
+          token = ((long)b * args.T + pos) * args.F + f;
+        } else {  // grp = b*T + t, pos = f
+          token = (long)grp * args.F + pos;
         }
+        const float scale = args.G[token * 8 + h] / l_run;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          o0[i] *= scale;
+          o1[i] *= scale;
+        }
+        TIn* dst = static_cast<TIn*>(args.O) + token * 512 + h * 64;
+        store32<TIn>(dst, o0);
+        store32<TIn>(dst + 32, o1);
       }
     }
   }

@@ -28,6 +28,6 @@ void launch_chunk_ola(const float* chunks, int64_t clen, const int64_t* d_starts
 cudaError_t launch_gemm(int epi, int precision, const CUtensorMap& map_a, const CUtensorMap& map_b,
                         const CUtensorMap* map_out, const GemmArgs& args, int num_sms, cudaStream_t st);
 cudaError_t launch_attention(int precision, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
-                             const AttnArgs& args, cudaStream_t st);
+                             const AttnArgs& args, int num_sms, cudaStream_t st);
 
 }  // namespace trc

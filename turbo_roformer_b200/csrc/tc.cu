@@ -55,13 +55,14 @@ cudaError_t launch_gemm_p(int epi, const CUtensorMap& ma, const CUtensorMap& mb,
 
 template <typename T>
 cudaError_t launch_attention_t(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
-                               const AttnArgs& args, cudaStream_t st) {
+                               const AttnArgs& args, int num_sms, cudaStream_t st) {
   auto kern = attention_kernel<T>;
   static std::atomic<unsigned long long> done{0};  // one per <T> instantiation
   cudaError_t e = allow_smem(kern, AttnSmem::kBytes, done);
   if (e != cudaSuccess) return e;
-  if (args.num_tiles <= 0) return cudaSuccess;
-  kern<<<args.num_tiles, kAttnThreads, AttnSmem::kBytes, st>>>(mq, mk, mv, args);
+  if (args.num_items <= 0) return cudaSuccess;
+  const int grid = args.num_items < num_sms ? args.num_items : num_sms;
+  kern<<<grid, kAttnThreads, AttnSmem::kBytes, st>>>(mq, mk, mv, args);
   return cudaGetLastError();
 }
 
@@ -74,9 +75,9 @@ cudaError_t launch_gemm(int epi, int precision, const CUtensorMap& ma, const CUt
 }
 
 cudaError_t launch_attention(int precision, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
-                             const AttnArgs& args, cudaStream_t st) {
-  return precision == 0 ? launch_attention_t<__half>(mq, mk, mv, args, st)
-                        : launch_attention_t<__nv_bfloat16>(mq, mk, mv, args, st);
+                             const AttnArgs& args, int num_sms, cudaStream_t st) {
+  return precision == 0 ? launch_attention_t<__half>(mq, mk, mv, args, num_sms, st)
+                        : launch_attention_t<__nv_bfloat16>(mq, mk, mv, args, num_sms, st);
 }
 
 }  // namespace trc
