@@ -268,28 +268,27 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         tc_fence_after();
         const int key0 = j * 128;
         const int kmax = freq ? 128 : min(128, args.L - key0);  // keys of this tile that exist
-        // pass 1: row maximum over the valid keys
-        float mx = -INFINITY;
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          float v[32];
-          tmem_ld32(tS + c * 32, v);
-          if (freq) {
+        // the whole score row in registers (one TMEM read); keys outside this row's sequence -> -inf
+        float sc[128];
+        tmem_ld128(tS, sc);
+        if (freq) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const int kc = c * 32 + i;
-              if ((kc >> 6) == my_block && (kc & 63) < args.L) mx = fmaxf(mx, v[i]);
-            }
-          } else if (c * 32 + 32 <= kmax) {
+          for (int i = 0; i < 128; ++i)
+            if ((i >> 6) != my_block || (i & 63) >= args.L) sc[i] = -INFINITY;
+        } else if (kmax < 128) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) mx = fmaxf(mx, v[i]);
-          } else {
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (c * 32 + i < kmax) mx = fmaxf(mx, v[i]);
-          }
+          for (int i = 0; i < 128; ++i)
+            if (i >= kmax) sc[i] = -INFINITY;
         }
-        const float m_tile = mx * kLog2e;
+        float mx4[4] = {sc[0], sc[1], sc[2], sc[3]};
+#pragma unroll
+        for (int i = 4; i < 128; i += 4) {
+          mx4[0] = fmaxf(mx4[0], sc[i]);
+          mx4[1] = fmaxf(mx4[1], sc[i + 1]);
+          mx4[2] = fmaxf(mx4[2], sc[i + 2]);
+          mx4[3] = fmaxf(mx4[3], sc[i + 3]);
+        }
+        const float m_tile = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * kLog2e;
         if (j == 0) {
           m_run = m_tile;
         } else {
@@ -308,26 +307,24 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             }
           }
         }
-        // pass 2: P = 2^(s log2e - m_run) as 16-bit pairs into the first 64 columns of S
-#pragma unroll 1
+        // P = 2^(s log2e - m_run) as 16-bit pairs into the first 64 columns of S
+        const float2 scale2 = make_float2(kLog2e, kLog2e);
+        const float2 shift2 = make_float2(-m_run, -m_run);
+        float2 l2 = make_float2(0.f, 0.f);
+#pragma unroll
         for (int c = 0; c < 4; ++c) {
-          float v[32];
-          tmem_ld32(tS + c * 32, v);
           uint32_t packed[16];
 #pragma unroll
           for (int i = 0; i < 32; i += 2) {
-            float p2[2];
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const int kc = c * 32 + i + e;
-              const bool kv = freq ? ((kc >> 6) == my_block && (kc & 63) < args.L) : (kc < kmax);
-              p2[e] = kv ? ex2_approx(fmaf(v[i + e], kLog2e, -m_run)) : 0.f;
-              l_run += p2[e];
-            }
-            packed[i >> 1] = OperandType<TIn>::pack2(p2[0], p2[1]);
+            const int k = c * 32 + i;
+            const float2 xv = __ffma2_rn(make_float2(sc[k], sc[k + 1]), scale2, shift2);
+            const float2 pv = make_float2(ex2_approx(xv.x), ex2_approx(xv.y));
+            l2 = __fadd2_rn(l2, pv);
+            packed[i >> 1] = OperandType<TIn>::pack2(pv.x, pv.y);
           }
           tmem_st16(tS + c * 16, packed);
         }
+        l_run += l2.x + l2.y;
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(&p_full[x]);

@@ -177,6 +177,7 @@ struct EpiCtx {
   bool leader;     // issues the TMA stores of its column half
   uint8_t* slabs;  // 4 staging slabs: [half][2]
   float* scratch;  // same memory, used by the residual-norm epilogue
+  float* tab;      // rotary rows of the current q/k tile (qkv epilogue only)
   int slot;        // next slab slot of this half (alternates 0, 1)
 };
 
@@ -206,8 +207,9 @@ __device__ __forceinline__ bool qkv_token(const GemmArgs& a, const TileCoord& tc
   return f < a.F && bt < a.M;
 }
 
+// Rotate 32 values (16 interleaved pairs (2j, 2j+1)) by the angles in cs[0..15], sn[0..15] (shared
+// memory, 16-byte aligned): x0 c - x1 s, x1 c + x0 s.
 __device__ __forceinline__ void rotate32(float (&v)[32], const float* cs, const float* sn) {
-  // interleaved pairs (2j, 2j+1) rotated by the angle of pair j: x0 c - x1 s, x1 c + x0 s
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     const float4 c4 = reinterpret_cast<const float4*>(cs)[q];
@@ -221,6 +223,27 @@ __device__ __forceinline__ void rotate32(float (&v)[32], const float* cs, const 
       v[2 * j] = x0 * cc[e] - x1 * ss[e];
       v[2 * j + 1] = x1 * cc[e] + x0 * ss[e];
     }
+  }
+}
+
+// Rotary table rows of a q/k tile, staged in shared memory once per tile by all epilogue warps:
+// [cos|sin][row][kTabStride floats]; the stride of 36 floats keeps each thread's 16-byte reads of its
+// own row free of bank conflicts. time mode: rows = frames t0..t0+127; freq mode: rows = bands 0..63.
+constexpr int kTabStride = 36;
+constexpr int kTabBytes = 2 * 128 * kTabStride * 4;
+
+__device__ __forceinline__ void load_rotary_rows(const GemmArgs& a, const TileCoord& tc, float* tab, int tid) {
+  const bool time = a.a_mode == A_TIME_SEQ;
+  const int L = time ? a.T : a.F;
+  const int rows = time ? 128 : 64;
+  const int pos0 = time ? tc.m0 : 0;
+  for (int k = tid; k < 2 * rows * 8; k += 32 * kEpiWarps) {
+    const int table = k / (rows * 8);
+    const int rem = k - table * rows * 8;
+    const int row = rem >> 3, q = rem & 7;
+    const int pos = min(pos0 + row, L - 1);
+    const float* src = (table == 0 ? a.cos_tab : a.sin_tab) + (size_t)pos * 32 + q * 4;
+    *reinterpret_cast<float4*>(tab + (table * 128 + row) * kTabStride + q * 4) = __ldg(reinterpret_cast<const float4*>(src));
   }
 }
 
@@ -247,11 +270,8 @@ __device__ __forceinline__ void epi_qkv(const GemmArgs& a, const TileCoord& tc, 
   const bool time = a.a_mode == A_TIME_SEQ;
   const int part = tc.n0 >> 9;  // 0 q, 1 k, 2 v
   const CUtensorMap* map = part == 0 ? mq : part == 1 ? mk : mv;
-  const int L = time ? a.T : a.F;
-  int pos = time ? tc.m0 + r : (r & 63);
-  pos = min(pos, L - 1);  // rows past the sequence end are clipped by the store; keep the table read in range
-  const float* cs = a.cos_tab + (size_t)pos * 32;
-  const float* sn = a.sin_tab + (size_t)pos * 32;
+  const float* cs = e.tab + (time ? r : (r & 63)) * kTabStride;
+  const float* sn = cs + 128 * kTabStride;
 #pragma unroll 1
   for (int hh = 0; hh < 2; ++hh) {
     const int hc = e.hf * 2 + hh;                    // head within the tile
@@ -412,7 +432,7 @@ __device__ __forceinline__ void epi_glu(const GemmArgs& a, const TileCoord& tc, 
 }
 
 // ------------------------------------------------------------------------------------------------ kernel
-template <int BN, int STAGES>
+template <int BN, int STAGES, int EPI>
 struct GemmSmem {
   static constexpr int kABytes = kGemmBM * kGemmBK * 2;  // 16 KB
   static constexpr int kBBytes = BN * kGemmBK * 2;       // 32 KB at BN = 256
@@ -420,7 +440,8 @@ struct GemmSmem {
   static constexpr int kOutOffset = STAGES * kStageBytes;  // 4 staging slabs / residual-norm scratch
   static constexpr int kOutBytes = 4 * kSlabBytes;
   static_assert(kEpiWarps * 32 * 33 * 4 + 2 * 256 * 4 <= kOutBytes, "residual-norm scratch must fit");
-  static constexpr int kBarOffset = kOutOffset + kOutBytes;
+  static constexpr int kTabOffset = kOutOffset + kOutBytes;  // rotary rows (qkv only)
+  static constexpr int kBarOffset = kTabOffset + (EPI == EPI_QKV ? kTabBytes : 0);
   static constexpr int kBytes = kBarOffset + 256 + 1024;  // + barriers + alignment slack
 };
 
@@ -429,7 +450,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                 const __grid_constant__ CUtensorMap map_o0, const __grid_constant__ CUtensorMap map_o1,
                 const __grid_constant__ CUtensorMap map_o2, const __grid_constant__ GemmArgs args) {
-  using S = GemmSmem<BN, STAGES>;
+  using S = GemmSmem<BN, STAGES, EPI>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kBarOffset);
@@ -568,12 +589,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     e.leader = (e.ewarp & 3) == 0 && lane == 0;
     e.slabs = smem + S::kOutOffset;
     e.scratch = reinterpret_cast<float*>(smem + S::kOutOffset);
+    e.tab = reinterpret_cast<float*>(smem + S::kTabOffset);
     e.slot = 0;
     int local = 0;
     for (int tile = blockIdx.x; tile < args.num_tiles; tile += gridDim.x, ++local) {
       const TileCoord tc = gemm_decode<BN>(args, tile);
       const int buf = local & 1;
       const uint32_t use = (uint32_t)(local >> 1);
+      if constexpr (EPI == EPI_QKV) {
+        if (tc.n0 < 1024) {  // q or k tile: stage its rotary rows (overlaps this tile's MMAs)
+          named_bar(3, 32 * kEpiWarps);  // every warp is done with the previous table
+          load_rotary_rows(args, tc, e.tab, e.ewarp * 32 + lane);
+          named_bar(3, 32 * kEpiWarps);
+        }
+      }
       // every epilogue warp takes the same decision, so no warp is left waiting at a named barrier
       const bool ok = mbar_wait_warp(&acc_full[buf], use & 1, args.err, kErrWaitEpilogue, abort_flag);
       if (!named_bar_and(4, 32 * kEpiWarps, ok)) break;
