@@ -12,7 +12,7 @@
 //   EPI_QKV       qkv_rope_gemm (:442-540): rotary on q,k in fp32, Q/K/V stored per head as TMA boxes of
 //                 the attention layout, sigmoid gates (16-column tile)
 //   EPI_RESNORM   gemm_res_norm (:543-586): X += acc (+ bias); xn = X / max(|X|, eps)
-//   EPI_GELU      gemm_gelu (:610-642):     H = gelu_erf(acc + b)
+//   EPI_GELU      gemm_gelu (:610-642):     H = gelu(acc + b), erf by A&S 7.1.28
 //   EPI_MASK_TANH mask MLP layer 1 (fast.py:354):  tanh(acc + b1) per band
 //   EPI_MASK_GLU  mask MLP layer 2 + GLU (fast.py:355-357): a * sigmoid(g), with (a, g) rows interleaved
 #pragma once
@@ -137,7 +137,35 @@ __device__ __forceinline__ TileCoord gemm_decode(const GemmArgs& a, int tile) {
 }
 
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + __expf(-x)); }
-__device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Exact-form GELU 0.5·x·(1 + erf(x/√2)) on a pair of values. erf(z), z >= 0, is Abramowitz & Stegun 7.1.28:
+// 1 - (1 + a1·z + ... + a6·z^6)^-16 (|error| <= 3e-7), one reciprocal per value and the polynomial in packed
+// fp32 pairs. The odd extension folds into 0.5·x + 0.5·|x|·erf(|x|/√2). The reference's CPU epilogue also
+// evaluates erf by an Abramowitz & Stegun rational form (kernels.cpp:588-607, formula 7.1.26).
+__device__ __forceinline__ float2 gelu_erf2(float2 x) {
+  const float2 ax = make_float2(fabsf(x.x), fabsf(x.y));
+  const float2 z = __fmul2_rn(ax, make_float2(0.70710678118654752f, 0.70710678118654752f));
+  float2 p = __ffma2_rn(make_float2(4.30638e-5f, 4.30638e-5f), z, make_float2(2.765672e-4f, 2.765672e-4f));
+  p = __ffma2_rn(p, z, make_float2(1.520143e-4f, 1.520143e-4f));
+  p = __ffma2_rn(p, z, make_float2(0.0092705272f, 0.0092705272f));
+  p = __ffma2_rn(p, z, make_float2(0.0422820123f, 0.0422820123f));
+  p = __ffma2_rn(p, z, make_float2(0.0705230784f, 0.0705230784f));
+  p = __ffma2_rn(p, z, make_float2(1.0f, 1.0f));
+  float2 r = make_float2(rcp_approx(p.x), rcp_approx(p.y));
+  r = __fmul2_rn(r, r);
+  r = __fmul2_rn(r, r);
+  r = __fmul2_rn(r, r);
+  r = __fmul2_rn(r, r);
+  const float2 erf_abs = __ffma2_rn(r, make_float2(-1.0f, -1.0f), make_float2(1.0f, 1.0f));
+  const float2 hx = __fmul2_rn(x, make_float2(0.5f, 0.5f));
+  const float2 hax = __fmul2_rn(ax, make_float2(0.5f, 0.5f));
+  return __ffma2_rn(hax, erf_abs, hx);
+}
 
 template <typename TIn>
 __device__ __forceinline__ void store32(TIn* dst, const float (&v)[32]) {
@@ -385,10 +413,20 @@ __device__ __forceinline__ void epi_act(const GemmArgs& a, const TileCoord& tc, 
       v0[4 * q] += b0.x; v0[4 * q + 1] += b0.y; v0[4 * q + 2] += b0.z; v0[4 * q + 3] += b0.w;
       v1[4 * q] += b1.x; v1[4 * q + 1] += b1.y; v1[4 * q + 2] += b1.z; v1[4 * q + 3] += b1.w;
     }
+    if (tanh_act) {
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      v0[i] = tanh_act ? tanhf(v0[i]) : gelu_erf(v0[i]);
-      v1[i] = tanh_act ? tanhf(v1[i]) : gelu_erf(v1[i]);
+      for (int i = 0; i < 32; ++i) {
+        v0[i] = tanhf(v0[i]);
+        v1[i] = tanhf(v1[i]);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; i += 2) {
+        const float2 g0 = gelu_erf2(make_float2(v0[i], v0[i + 1]));
+        const float2 g1 = gelu_erf2(make_float2(v1[i], v1[i + 1]));
+        v0[i] = g0.x; v0[i + 1] = g0.y;
+        v1[i] = g1.x; v1[i + 1] = g1.y;
+      }
     }
     stage_slab_row<TIn>(slab, e.row, v0, v1);
     slab_release(e);
