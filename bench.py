@@ -40,14 +40,15 @@ METRIC = "audio-sec separated/sec"
 UNIT = "audio-s/s"
 PUBLISHED = 1.38  # reference, 252.39 s song / 183.0 s wall on 8 Zen 4 cores (docs/benchmarks.md:71)
 
-# DRAM traffic per unit of work measured by ncu for each section's kernel (bytes per token-layer, or per
-# chunk for the DSP stages); see profiles/*.md for the captures. None = not captured.
-TRAFFIC_PER_TOKEN = {
-    "attention_t": (327.8e6 + 91.8e6) / 105_462,
-    "attention_f": (327.4e6 + 87.3e6) / 105_462,
-    "qkv_rope_gemm": (55.7e6 + 274.9e6) / 105_462,
-    "gemm_ff1": (54.6e6 + 162.5e6) / 105_462,
-    "gemm_out_res_norm": (217.0e6 + 109.7e6) / 105_462,
+# DRAM bytes (read + write) of one launch on ONE chunk (1700 frames x 62 bands = 105,400 tokens), from
+# `ncu --set full` on `bench.py --batch 1` (profiles/attention_kernel_chunk.md, profiles/gemm_kernel_chunk.md);
+# a batched launch moves this per chunk. None = not captured.
+TRAFFIC_PER_CHUNK = {
+    "attention_t": (328.19e6 + 87.67e6),
+    "attention_f": (327.61e6 + 82.77e6),
+    "qkv_rope_gemm": (55.33e6 + 268.42e6),
+    "gemm_out_res_norm": (216.23e6 + 106.42e6),
+    "gemm_ff1": (54.60e6 + 156.31e6),
 }
 
 
@@ -240,7 +241,6 @@ def main() -> None:
 
     # ---------------------------------------------------------------- timed region (device-resident song)
     clocks = ClockSampler(local)
-    _lib.check(lib.trc_profile(sep.net.handle, 1))
     launches0 = lib.trc_launch_count()
     torch.cuda.synchronize()
     barrier()
@@ -254,6 +254,13 @@ def main() -> None:
     ms = e0.elapsed_time(e1)
     launches = lib.trc_launch_count() - launches0
     clk = clocks.stop()
+
+    # ---------------------------------------------------------------- per-section device time (one extra song)
+    # Sections are bracketed by CUDA events inside the library; they run outside the timed region so the
+    # event records cost the headline number nothing.
+    _lib.check(lib.trc_profile(sep.net.handle, 1))
+    step()
+    torch.cuda.synchronize()
     buf = ctypes.create_string_buffer(8192)
     _lib.check(lib.trc_profile_read(sep.net.handle, buf, 8192))
     _lib.check(lib.trc_profile(sep.net.handle, 0))
@@ -261,6 +268,7 @@ def main() -> None:
     for line in buf.value.decode().strip().splitlines():
         name, tms, cnt = line.split()
         sections[name] = (float(tms), int(cnt))
+    barrier()
     if world > 1:
         t = torch.tensor([ms, float(launches)], device=dev, dtype=torch.float64)
         tmax = t.clone()
@@ -270,27 +278,36 @@ def main() -> None:
     value = args.steps * SONG_SECONDS / (ms / 1e3)
 
     # ---------------------------------------------------------------- e2e through the public API
+    # N=1: Separator.separate(mix) on a song held in pinned host memory, numpy in and numpy out: the host
+    # checks, one H2D copy, peak gain, all chunks, overlap-add and one D2H copy, timed by the host clock
+    # around the calls. N>1: each rank copies the song from pinned memory, runs its shard, and rank 0
+    # copies the gathered result back; device time, max over ranks.
     pinned = torch.from_numpy(song).pin_memory()
-    out_host = torch.empty(2, n, dtype=torch.float32).pin_memory()
+    song_pinned = pinned.numpy()
     barrier()
     torch.cuda.synchronize()
-    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    f0.record()
-    for _ in range(args.steps):
-        xs = pinned.to(dev, non_blocking=True)
-        xs_np_gain = gain  # same peak gain as the host path computes (prepare_44k on the host song)
-        if xs_np_gain != 1.0:
-            xs.mul_(np.float32(xs_np_gain))
-        if world > 1:
+    if world == 1:
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            y_host = sep.separate(song_pinned, overlap=OVERLAP)
+        torch.cuda.synchronize()
+        ms_e2e = 1e3 * (time.perf_counter() - t0)
+        assert y_host.shape == song.shape
+    else:
+        out_host = torch.empty(2, n, dtype=torch.float32).pin_memory()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record()
+        for _ in range(args.steps):
+            xs = pinned.to(dev, non_blocking=True)
+            if gain != 1.0:
+                xs.mul_(np.float32(gain))
             y = separate_song_cuda(sep, xs, OVERLAP)
-        else:
-            y = sep.separate_device(xs, OVERLAP)
-        if y is not None:
-            out_host.copy_(y, non_blocking=True)
-    f1.record()
-    torch.cuda.synchronize()
+            if y is not None:
+                out_host.copy_(y, non_blocking=True)
+        f1.record()
+        torch.cuda.synchronize()
+        ms_e2e = f0.elapsed_time(f1)
     barrier()
-    ms_e2e = f0.elapsed_time(f1)
     if world > 1:
         t = torch.tensor([ms_e2e], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -303,18 +320,21 @@ def main() -> None:
     roofline = None
     if dom is not None:
         bound, work = section_work(dom, T * F, T, F)
-        n_layer_chunks = args.steps * len(starts) * cfg.depth  # chunk-layers processed by this rank (N=1)
-        if world > 1:
-            n_layer_chunks = None
+        # units of `work` this rank ran in the profiled song: its chunks x blocks per chunk (the time and
+        # frequency attention sections run once per layer, the GEMM sections once per transformer block)
+        from turbo_roformer_b200.distributed import shard_bounds
+
+        lo, hi = shard_bounds(len(starts), world)[rank] if world > 1 else (0, len(starts))
+        units = (hi - lo) * (cfg.depth if dom.startswith("attention") else 2 * cfg.depth)
         tot_ms, cnt = sections[dom]
-        if n_layer_chunks:
-            achieved = work * n_layer_chunks / (tot_ms / 1e3) / 1e12
-            tr = TRAFFIC_PER_TOKEN.get(dom)
+        if units:
+            achieved = work * units / (tot_ms / 1e3) / 1e12
+            tr = TRAFFIC_PER_CHUNK.get(dom)
             roofline = {
                 "kernel": dom, "bound": bound, "achieved": achieved, "peak": pk["tc_sustained"], "unit": "TFLOP/s",
                 "frac": achieved / pk["tc_sustained"],
                 "peak_kind": f"bf16 dense sustained, {pk['src']} (MEASURED_PEAKS.json)",
-                "traffic": tr * T * F if tr else None, "traffic_unit": "bytes per chunk-layer launch share",
+                "traffic": tr * units / cnt if tr else None, "traffic_unit": "DRAM bytes per launch",
                 "launches": cnt, "avg_launch_ms": tot_ms / cnt,
             }
 
@@ -330,7 +350,7 @@ def main() -> None:
         "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": song.nbytes * world,
                 "d2h_bytes_per_step": song.nbytes},
         "gpu_launches": launches, "clocks": clk, "roofline": roofline,
-        "sections_ms": {k: round(v[0] / args.steps, 3) for k, v in sorted(sections.items())},
+        "sections_ms": {k: round(v[0], 3) for k, v in sorted(sections.items())},
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         t_cpu, y_cpu = cpu_chunk_time(sd, cfg, np.ascontiguousarray(xp[:, :chunk]))

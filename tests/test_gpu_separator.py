@@ -99,6 +99,13 @@ def test_progress_and_invalid_arguments(sep):
         sep.separate(mix, sr=0)
     with pytest.raises(ValueError):
         sep.separate(np.zeros((2, 10), np.int16))
+    # the NaN/inf scan runs on the device: the call still raises and the handle stays usable
+    for bad in (np.nan, np.inf, -np.inf):
+        m = mix.copy()
+        m[1, 1234] = bad
+        with pytest.raises(ValueError):
+            sep.separate(m)
+    np.testing.assert_array_equal(sep.separate(mix), sep.separate(mix))
 
 
 def test_concurrent_calls_are_serialised(sep):

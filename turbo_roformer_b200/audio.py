@@ -14,8 +14,15 @@ import numpy as np
 MAX_CHANNELS = 16
 
 
-def as_channels_first(mix) -> np.ndarray:
-    """Validate and convert to float32 (channels, samples); raises ValueError like audio.py:16-32."""
+def check_finite(a: np.ndarray) -> None:
+    if not np.isfinite(a).all():
+        raise ValueError("input contains NaN or inf samples")
+
+
+def as_channels_first(mix, finite: bool = True) -> np.ndarray:
+    """Validate and convert to float32 (channels, samples); raises ValueError like audio.py:16-32.
+
+    ``finite=False`` leaves the NaN/inf scan to the caller (the CUDA separator runs it on the device)."""
     a = np.asarray(mix)
     if a.dtype.kind != "f":
         raise ValueError(f"expected a floating point array (got dtype {a.dtype}); scale integer PCM to [-1, 1] first")
@@ -28,8 +35,8 @@ def as_channels_first(mix) -> np.ndarray:
     if a.shape[0] == 0 or a.shape[1] == 0:
         raise ValueError("empty input")
     a = a.astype(np.float32, copy=False)
-    if not np.isfinite(a).all():
-        raise ValueError("input contains NaN or inf samples")
+    if finite:
+        check_finite(a)
     return a
 
 

@@ -171,12 +171,17 @@ class Separator:
         C = min(self.chunk, n_samples)
         return len(chunk_starts(n_samples, C, step_for(C, overlap)))
 
-    def prepare_44k(self, x: np.ndarray) -> tuple[np.ndarray, float]:
-        """Short-clip padding and peak gain (separator.py:190-197): returns (padded x * gain, gain)."""
+    def _pad_short(self, x: np.ndarray) -> np.ndarray:
+        """Clips shorter than one chunk are zero-padded to whole hops, at least 3 (separator.py:190-193)."""
         n0 = x.shape[1]
         if n0 < self.chunk and (n0 % self.hop or n0 < 3 * self.hop):
             target = max(-(-n0 // self.hop) * self.hop, 3 * self.hop)
             x = np.pad(x, ((0, 0), (0, target - n0)))
+        return x
+
+    def prepare_44k(self, x: np.ndarray) -> tuple[np.ndarray, float]:
+        """Short-clip padding and peak gain (separator.py:190-197): returns (padded x * gain, gain)."""
+        x = self._pad_short(x)
         peak = float(np.abs(x).max())
         gain = PEAK / peak if peak > PEAK else 1.0
         return np.ascontiguousarray(x * np.float32(gain) if gain != 1.0 else x), gain
@@ -187,13 +192,22 @@ class Separator:
 
     @torch.inference_mode()
     def _separate_44k(self, x: np.ndarray, overlap: float, progress) -> np.ndarray:
+        """separator.py:186-200 with the peak gain and the NaN/inf scan on the device: the caller's samples
+        are copied to the GPU once (at DMA speed when they live in pinned memory), the gain
+        PEAK / max|x| (rounded from double to float32, as the host code computes it) multiplies the mix
+        and divides the instrumental there, and one device-to-host copy returns the result."""
         n0 = x.shape[1]
-        xp, gain = self.prepare_44k(x)
-        xt = torch.from_numpy(xp).to(self.device)
-        inst = self.separate_device(xt, overlap, progress).cpu()
-        if gain != 1.0:
-            inst.div_(gain)
-        return np.ascontiguousarray(inst.numpy()[:, :n0])
+        xd = torch.from_numpy(np.ascontiguousarray(self._pad_short(x))).to(self.device, non_blocking=True)
+        peak = xd.abs().amax()
+        finite = torch.isfinite(peak)  # max|x| is finite iff every sample is (NaN propagates through amax)
+        gain = torch.where(peak > PEAK, (PEAK / peak.double()).float(), torch.ones((), device=xd.device))
+        xd.mul_(gain)
+        inst = self.separate_device(xd, overlap, progress)
+        inst.div_(gain)
+        out = inst.cpu()
+        if not bool(finite):
+            raise ValueError("input contains NaN or inf samples")
+        return np.ascontiguousarray(out.numpy()[:, :n0])
 
     def separate(
         self,
@@ -208,9 +222,10 @@ class Separator:
         if int(sr) <= 0:
             raise ValueError("sr must be positive")
         sr = int(sr)
-        x = audio.to_stereo(audio.as_channels_first(mix))
+        x = audio.to_stereo(audio.as_channels_first(mix, finite=False))
         n = x.shape[1]
         if sr != SR:
+            audio.check_finite(x)
             x = audio.resample(x, sr, SR, length=max(1, round(n * SR / sr)))
         with self._lock:
             if self.threads:
