@@ -5,14 +5,16 @@
 // softmax over the keys, O = P V, then x sigmoid gate, head merge and scatter back to token order.
 // The reference keeps whole score rows (two passes); here a CTA owns two 128-row query tiles (A, B)
 // and streams 128-key tiles:
-//   * S = Q K^T (both operands in shared memory) lands in TMEM; the softmax warpgroup of the tile reads
-//     it, writes unnormalised 16-bit P back into the same TMEM columns, and the tensor core computes
-//     O += P V with P read straight from TMEM (no shared-memory round trip for P).
-//   * O accumulates in TMEM. The running row maximum is only raised when a tile's maximum exceeds it
-//     by more than 2^8 (then O and the row sum are rescaled in place); P <= 2^8 keeps 16-bit P exact
-//     enough and the final O / l is the exact softmax average.
-//   * The MMA issuer ping-pongs between the tiles (PV_A, S_A next, PV_B, S_B next) so one tile's
-//     softmax overlaps the other tile's matrix products.
+//   * S = Q K^T (both operands in shared memory) lands in TMEM. The softmax warps of the tile read the
+//     whole score row into registers at once, which frees the S columns: the next key tile's S is
+//     issued right then and runs on the tensor core while this tile's exponentials are computed.
+//   * Unnormalised 16-bit P goes to its own TMEM columns and the tensor core computes O += P V with P
+//     read straight from TMEM (no shared-memory round trip for P). O accumulates in TMEM.
+//   * The running row maximum is only raised when a tile's maximum exceeds it by more than 2^8 (then O
+//     and the row sum are rescaled in place); P <= 2^8 keeps 16-bit P exact enough and the final O / l
+//     is the exact softmax average.
+//   * The MMA issuer is an event loop over both tiles: it issues whichever product has its inputs
+//     ready (next S once the softmax has taken the previous one, P V once P is written).
 //   * Persistent CTAs walk the work items; Q is double buffered so the next item's first products
 //     start while the current item's epilogue runs.
 //
@@ -55,9 +57,11 @@ struct AttnSmem {
   static constexpr int kBytes = kBar + 512 + 1024;
 };
 
-// TMEM columns: S_A [0,128), S_B [128,256) (P aliases their first 64 columns), O_A [256,320), O_B [320,384)
+// TMEM columns (all 512): S_A [0,128), S_B [128,256), P_A [256,320), P_B [320,384) (16-bit pairs),
+// O_A [384,448), O_B [448,512)
 __device__ __forceinline__ uint32_t tmem_col_s(int x) { return (uint32_t)x * 128u; }
-__device__ __forceinline__ uint32_t tmem_col_o(int x) { return 256u + (uint32_t)x * 64u; }
+__device__ __forceinline__ uint32_t tmem_col_p(int x) { return 256u + (uint32_t)x * 64u; }
+__device__ __forceinline__ uint32_t tmem_col_o(int x) { return 384u + (uint32_t)x * 64u; }
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: P stays <= 2^8
 
 template <typename TIn>
@@ -72,10 +76,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t* q_empty = q_full + 2;            // [2]
   uint64_t* kv_full = q_empty + 2;           // [stages]
   uint64_t* kv_empty = kv_full + kAttnKvStages;
-  uint64_t* s_full = kv_empty + kAttnKvStages;  // [2] per query tile
-  uint64_t* p_full = s_full + 2;                // [2]
-  uint64_t* o_full = p_full + 2;                // [2]
-  uint64_t* o_free = o_full + 2;                // [2]
+  uint64_t* s_full = kv_empty + kAttnKvStages;  // [2] per query tile: S in TMEM (MMA commit)
+  uint64_t* s_free = s_full + 2;                // [2] S read into registers (one arrive per softmax warp)
+  uint64_t* p_full = s_free + 2;                // [2] P written, O rescaled (one arrive per softmax warp)
+  uint64_t* p_free = p_full + 2;                // [2] O += P V done: P reusable, O current (MMA commit)
+  uint64_t* o_free = p_free + 2;                // [2] epilogue has read O (one arrive per softmax warp)
   uint64_t* drain = o_free + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -91,9 +96,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_init(&q_full[b], 1);
       mbar_init(&q_empty[b], 1);
       mbar_init(&s_full[b], 1);
-      mbar_init(&p_full[b], 128);
-      mbar_init(&o_full[b], 1);
-      mbar_init(&o_free[b], 128);
+      mbar_init(&s_free[b], 4);
+      mbar_init(&p_full[b], 4);
+      mbar_init(&p_free[b], 1);
+      mbar_init(&o_free[b], 4);
     }
     for (int s = 0; s < kAttnKvStages; ++s) {
       mbar_init(&kv_full[s], 1);
@@ -179,57 +185,90 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const uint32_t idesc_qk = idesc_f16(128, 128, OperandType<TIn>::kFormat, 0, 0);
       const uint32_t idesc_pv = idesc_f16(128, 64, OperandType<TIn>::kFormat, 0, 1);  // V is MN-major
       int kvc = 0, local = 0;
-      int steps[2] = {0, 0};  // S tiles issued per query tile (s_full / p_full phase counters)
+      uint32_t s_iss[2] = {0, 0};   // S tiles issued per query tile, all items (s_full / s_free phases)
+      uint32_t pv_iss[2] = {0, 0};  // P V products issued per query tile (p_full / p_free phases)
       bool ok = true;
-      auto wait = [&](uint64_t* bar, uint32_t parity) {
-        if (ok && !mbar_wait(bar, parity, args.err, kErrWaitMma, abort_flag)) ok = false;
-        return ok;
-      };
       for (int item = blockIdx.x; item < args.num_items && ok; item += gridDim.x, ++local) {
         const int qb = local & 1;
-        if (!wait(&q_full[qb], (uint32_t)(local >> 1) & 1)) break;
-        const uint32_t sq = smem_u32(smem + S::kQ + qb * 2 * S::kTile);
-        auto kv_index = [&](int x, int j) { return freq ? kvc + x : kvc + j; };
-        auto issue_s = [&](int x, int j) {
-          const int idx = kv_index(x, j);
-          const int st = idx % kAttnKvStages;
-          if ((x == 0 || freq) && !wait(&kv_full[st], (uint32_t)(idx / kAttnKvStages) & 1)) return;
-          tc_fence_after();
-          const uint32_t sk = smem_u32(smem + S::kKV + st * 2 * S::kTile);
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint64_t ad = sdesc_sw128(sq + x * S::kTile + kk * 32, 16, 1024);
-            const uint64_t bd = sdesc_sw128(sk + kk * 32, 16, 1024);
-            mma_f16_ss(tmem_base + tmem_col_s(x), ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
-          }
-          mma_commit(&s_full[x]);
-          ++steps[x];
-        };
-        auto issue_pv = [&](int x, int j) {
-          if (!wait(&p_full[x], (uint32_t)(steps[x] - 1) & 1)) return;
-          if (j == 0 && local > 0 && !wait(&o_free[x], (uint32_t)(local - 1) & 1)) return;
-          tc_fence_after();
-          const int idx = kv_index(x, j);
-          const int st = idx % kAttnKvStages;
-          const uint32_t sv = smem_u32(smem + S::kKV + st * 2 * S::kTile + S::kTile);
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {  // 16 keys per MMA: P columns kk*8.., V rows kk*16..
-            const uint64_t bd = sdesc_sw128(sv + kk * 2048, 8192, 1024);
-            mma_f16_ts(tmem_base + tmem_col_o(x), tmem_base + tmem_col_s(x) + kk * 8, bd, idesc_pv,
-                       (j > 0 || kk > 0) ? 1u : 0u);
-          }
-          if (j == nsteps - 1) mma_commit(&o_full[x]);
-          if (x == 1 || freq) mma_commit(&kv_empty[st]);  // last reader of this key/value stage
-        };
-        issue_s(0, 0);
-        issue_s(1, 0);
-        for (int j = 0; j < nsteps && ok; ++j) {
-          issue_pv(0, j);
-          if (j + 1 < nsteps) issue_s(0, j + 1);
-          issue_pv(1, j);
-          if (j + 1 < nsteps) issue_s(1, j + 1);
+        if (!mbar_wait(&q_full[qb], (uint32_t)(local >> 1) & 1, args.err, kErrWaitMma, abort_flag)) {
+          ok = false;
+          break;
         }
-        mma_commit(&q_empty[qb]);
+        const uint32_t sq = smem_u32(smem + S::kQ + qb * 2 * S::kTile);
+        int s_next[2] = {0, 0}, p_next[2] = {0, 0};  // per tile: next S / next P V step of this item
+        uint64_t idle_since = 0;
+        uint32_t spins = 0;
+        while (p_next[0] < nsteps || p_next[1] < nsteps) {
+          bool progress = false;
+#pragma unroll
+          for (int x = 0; x < 2; ++x) {
+            // O += P V once the softmax has written P for this step
+            if (ok && p_next[x] < s_next[x] && mbar_test(&p_full[x], pv_iss[x] & 1u)) {
+              const int j = p_next[x];
+              if (j == 0 && local > 0 &&
+                  !mbar_wait(&o_free[x], (uint32_t)(local - 1) & 1, args.err, kErrWaitMma, abort_flag)) {
+                ok = false;
+              } else {
+                tc_fence_after();
+                const int idx = freq ? kvc + x : kvc + j;
+                const int st = idx % kAttnKvStages;
+                const uint32_t sv = smem_u32(smem + S::kKV + st * 2 * S::kTile + S::kTile);
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk) {  // 16 keys per MMA: P columns kk*8.., V rows kk*16..
+                  const uint64_t bd = sdesc_sw128(sv + kk * 2048, 8192, 1024);
+                  mma_f16_ts(tmem_base + tmem_col_o(x), tmem_base + tmem_col_p(x) + kk * 8, bd, idesc_pv,
+                             (j > 0 || kk > 0) ? 1u : 0u);
+                }
+                mma_commit(&p_free[x]);
+                // the stage's last reader: its own P V in freq mode, the later of the two tiles in time mode
+                if (freq || p_next[x ^ 1] > j) mma_commit(&kv_empty[st]);
+                ++p_next[x];
+                ++pv_iss[x];
+                progress = true;
+              }
+            }
+            // next S once the softmax has taken the previous one out of TMEM and its keys are loaded
+            if (ok && s_next[x] < nsteps && (s_iss[x] == 0 || mbar_test(&s_free[x], (s_iss[x] - 1) & 1u))) {
+              const int j = s_next[x];
+              const int idx = freq ? kvc + x : kvc + j;
+              const int st = idx % kAttnKvStages;
+              if (mbar_test(&kv_full[st], (uint32_t)(idx / kAttnKvStages) & 1)) {
+                tc_fence_after();
+                const uint32_t sk = smem_u32(smem + S::kKV + st * 2 * S::kTile);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+                  const uint64_t ad = sdesc_sw128(sq + x * S::kTile + kk * 32, 16, 1024);
+                  const uint64_t bd = sdesc_sw128(sk + kk * 32, 16, 1024);
+                  mma_f16_ss(tmem_base + tmem_col_s(x), ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
+                }
+                mma_commit(&s_full[x]);
+                ++s_next[x];
+                ++s_iss[x];
+                if (s_next[0] == nsteps && s_next[1] == nsteps) mma_commit(&q_empty[qb]);  // Q read
+                progress = true;
+              }
+            }
+          }
+          if (!ok) break;
+          // bounded: no progress for kWaitLimitNs (or another role aborted) ends the kernel with an error
+          if (progress) {
+            idle_since = 0;
+          } else if ((++spins & 63u) == 0) {
+            if (*abort_flag) {
+              ok = false;
+              break;
+            }
+            const uint64_t now = global_ns();
+            if (idle_since == 0) {
+              idle_since = now;
+            } else if (now - idle_since > kWaitLimitNs) {
+              record_error(args.err, kErrWaitMma);
+              *abort_flag = 1;
+              ok = false;
+              break;
+            }
+          }
+        }
         kvc += kv_per_item;
       }
       mma_commit(drain);
@@ -244,10 +283,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const int r = quarter * 32 + lane;  // query row within the tile
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const uint32_t tS = tmem_base + lane_off + tmem_col_s(x);
+    const uint32_t tP = tmem_base + lane_off + tmem_col_p(x);
     const uint32_t tO = tmem_base + lane_off + tmem_col_o(x);
     const float kLog2e = 1.4426950408889634f;
-    int step = 0, local = 0;
-    for (int item = blockIdx.x; item < args.num_items; item += gridDim.x, ++local) {
+    uint32_t g = 0;  // steps of this tile so far, all items (s_full / p_free phases)
+    for (int item = blockIdx.x; item < args.num_items; item += gridDim.x) {
       int seq, pos;
       if (freq) {
         seq = 4 * item + 2 * x + (r >> 6);
@@ -260,17 +300,21 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const int my_block = r >> 6;
       float m_run = -INFINITY, l_run = 0.f;
       bool ok = true;
-      for (int j = 0; j < nsteps; ++j, ++step) {
-        if (!mbar_wait_warp(&s_full[x], (uint32_t)step & 1, args.err, kErrWaitSoftmax, abort_flag)) {
+      for (int j = 0; j < nsteps; ++j, ++g) {
+        if (!mbar_wait_warp(&s_full[x], g & 1u, args.err, kErrWaitSoftmax, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const int key0 = j * 128;
-        const int kmax = freq ? 128 : min(128, args.L - key0);  // keys of this tile that exist
-        // the whole score row in registers (one TMEM read); keys outside this row's sequence -> -inf
+        // the whole score row in registers (one TMEM read); the S columns are then free for the next S
         float sc[128];
         tmem_ld128(tS, sc);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_free[x]);
+        // keys outside this row's sequence -> -inf
+        const int key0 = j * 128;
+        const int kmax = freq ? 128 : min(128, args.L - key0);  // keys of this tile that exist
         if (freq) {
 #pragma unroll
           for (int i = 0; i < 128; ++i)
@@ -282,38 +326,32 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
         float mx4[4] = {sc[0], sc[1], sc[2], sc[3]};
 #pragma unroll
-        for (int i = 4; i < 128; i += 4) {
-          mx4[0] = fmaxf(mx4[0], sc[i]);
-          mx4[1] = fmaxf(mx4[1], sc[i + 1]);
-          mx4[2] = fmaxf(mx4[2], sc[i + 2]);
-          mx4[3] = fmaxf(mx4[3], sc[i + 3]);
+        for (int i = 4; i < 124; i += 8) {
+          mx4[0] = fmax3(mx4[0], sc[i], sc[i + 4]);
+          mx4[1] = fmax3(mx4[1], sc[i + 1], sc[i + 5]);
+          mx4[2] = fmax3(mx4[2], sc[i + 2], sc[i + 6]);
+          mx4[3] = fmax3(mx4[3], sc[i + 3], sc[i + 7]);
         }
-        const float m_tile = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * kLog2e;
+        const float m_tile =
+            fmaxf(fmax3(mx4[0], mx4[1], sc[124]), fmax3(mx4[2], mx4[3], fmax3(sc[125], sc[126], sc[127]))) *
+            kLog2e;
+        bool rescale = false;
+        float alpha = 1.0f;
         if (j == 0) {
           m_run = m_tile;
         } else {
           const bool need = m_tile > m_run + kRescaleThreshold;
-          if (__any_sync(0xffffffffu, need)) {  // rescale O and l in place (O holds the steps < j)
-            const float alpha = need ? ex2_approx(m_run - m_tile) : 1.0f;
-            if (need) m_run = m_tile;
-            l_run *= alpha;
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              float o[32];
-              tmem_ld32(tO + h * 32, o);
-#pragma unroll
-              for (int i = 0; i < 32; ++i) o[i] *= alpha;
-              tmem_st32(tO + h * 32, o);
-            }
+          rescale = __any_sync(0xffffffffu, need);
+          if (need) {
+            alpha = ex2_approx(m_run - m_tile);
+            m_run = m_tile;
           }
         }
-        // P = 2^(s log2e - m_run) as 16-bit pairs into the first 64 columns of S
+        // P = 2^(s log2e - m_run) as 16-bit pairs, 32 keys at a time
         const float2 scale2 = make_float2(kLog2e, kLog2e);
         const float2 shift2 = make_float2(-m_run, -m_run);
         float2 l2 = make_float2(0.f, 0.f);
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t packed[16];
+        auto exp_chunk = [&](int c, uint32_t(&packed)[16]) {
 #pragma unroll
           for (int i = 0; i < 32; i += 2) {
             const int k = c * 32 + i;
@@ -322,22 +360,51 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             l2 = __fadd2_rn(l2, pv);
             packed[i >> 1] = OperandType<TIn>::pack2(pv.x, pv.y);
           }
-          tmem_st16(tS + c * 16, packed);
+        };
+        {
+          uint32_t packed[16];
+          exp_chunk(0, packed);
+          // P and O are this tile's again once the previous O += P V has completed
+          if (g > 0 && !mbar_wait_warp(&p_free[x], (g - 1) & 1u, args.err, kErrWaitSoftmax, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (rescale) {  // O holds the steps < j; 16 columns at a time (register budget)
+#pragma unroll 1
+            for (int h = 0; h < 4; ++h) {
+              float o[16];
+              uint32_t u[16];
+              tmem_ld16(tO + h * 16, o);
+#pragma unroll
+              for (int i = 0; i < 16; ++i) u[i] = __float_as_uint(o[i] * alpha);
+              tmem_st16(tO + h * 16, u);
+            }
+          }
+          tmem_st16(tP, packed);
         }
-        l_run += l2.x + l2.y;
+#pragma unroll
+        for (int c = 1; c < 4; ++c) {
+          uint32_t packed[16];
+          exp_chunk(c, packed);
+          tmem_st16(tP + c * 16, packed);
+        }
+        l_run = l_run * alpha + (l2.x + l2.y);
         tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(&p_full[x]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[x]);
       }
       if (!ok) break;
-      // epilogue: out = O / l * gate -> O[token][h*64 + d]
-      if (!mbar_wait_warp(&o_full[x], (uint32_t)local & 1, args.err, kErrWaitSoftmax, abort_flag)) break;
+      // epilogue: O is final once the last O += P V completed; out = O / l * gate -> O[token][h*64 + d]
+      if (!mbar_wait_warp(&p_free[x], (g - 1) & 1u, args.err, kErrWaitSoftmax, abort_flag)) break;
       tc_fence_after();
       float o0[32], o1[32];
       tmem_ld32(tO, o0);
       tmem_ld32(tO + 32, o1);
       tc_fence_before();
-      mbar_arrive(&o_free[x]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&o_free[x]);
       const bool valid = pos < args.L && seq < args.BH;
       if (valid) {
         const int h = seq & 7;
