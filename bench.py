@@ -228,7 +228,7 @@ def main() -> None:
     def step():
         if world > 1:
             return separate_song_cuda(sep, x_dev, OVERLAP)
-        return sep.separate_device(x_dev, OVERLAP)
+        return sep.separate_device(x_dev, OVERLAP, check=False)  # errors are checked after the timed region
 
     def barrier():
         if world > 1:
@@ -244,14 +244,16 @@ def main() -> None:
     launches0 = lib.trc_launch_count()
     torch.cuda.synchronize()
     barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.steps):
+    marks = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    marks[0].record()
+    for k in range(args.steps):
         step()
-    e1.record()
+        marks[k + 1].record()
     torch.cuda.synchronize()
     barrier()
-    ms = e0.elapsed_time(e1)
+    sep.net.check()  # raises if any kernel of the timed songs reported a device-side error
+    ms = marks[0].elapsed_time(marks[-1])
+    step_ms = [round(marks[k].elapsed_time(marks[k + 1]), 1) for k in range(args.steps)]
     launches = lib.trc_launch_count() - launches0
     clk = clocks.stop()
 
@@ -340,7 +342,7 @@ def main() -> None:
 
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
+        "ms_per_step": ms / args.steps, "step_ms": step_ms, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": value / PUBLISHED, "dtype": "f16", "data": "synthetic",
         "config": {"workload": "song_252s_overlap2_29chunks", "song_samples": n, "chunk_samples": chunk,
                    "frames_per_chunk": T, "chunks": len(starts), "chunks_per_forward": args.batch,

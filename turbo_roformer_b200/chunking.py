@@ -105,8 +105,12 @@ def ola_device(chunks: torch.Tensor, starts: list[int], chunk: int, n: int, out:
 
 
 def run_chunks(model, x: torch.Tensor, starts: list[int], C: int, batch: int, out: torch.Tensor,
-               progress: Callable[[int, int], None] | None = None, total: int | None = None, done0: int = 0) -> None:
-    """Forward the chunks x[:, s:s+C] for s in starts through ``model`` in batches, into out[i]."""
+               progress: Callable[[int, int], None] | None = None, total: int | None = None, done0: int = 0,
+               check: bool = True) -> None:
+    """Forward the chunks x[:, s:s+C] for s in starts through ``model`` in batches, into out[i].
+
+    ``check=False`` leaves the device-error check (a stream synchronisation) to the caller, so a caller
+    that queues several songs keeps the GPU fed while the host runs ahead."""
     total = total if total is not None else len(starts)
     for b0 in range(0, len(starts), batch):
         sel = starts[b0 : b0 + batch]
@@ -115,7 +119,8 @@ def run_chunks(model, x: torch.Tensor, starts: list[int], C: int, batch: int, ou
         if progress is not None:
             torch.cuda.current_stream(x.device).synchronize()
             progress(done0 + b0 + len(sel), total)
-    model.check()
+    if check:
+        model.check()
 
 
 def overlap_add_cuda(
@@ -125,6 +130,7 @@ def overlap_add_cuda(
     overlap: float,
     batch: int = 4,
     progress: Callable[[int, int], None] | None = None,
+    check: bool = True,
 ) -> torch.Tensor:
     """Device overlap-add: x (2, n) float32 on the model's GPU -> (2, n) on the same GPU."""
     n = x.shape[1]
@@ -132,5 +138,5 @@ def overlap_add_cuda(
     starts = chunk_starts(n, C, step_for(C, overlap))
     L = model.output_length(C)
     outs = torch.empty(len(starts), 2, L, device=x.device, dtype=torch.float32)
-    run_chunks(model, x, starts, C, batch, outs, progress)
+    run_chunks(model, x, starts, C, batch, outs, progress, check=check)
     return ola_device(outs, starts, C, n)

@@ -12,6 +12,7 @@
 #include <cstring>
 #include <map>
 #include <memory>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -931,6 +932,35 @@ int trc_profile_read(trc_handle* h, char* buf, int buflen) {
 
 long long trc_launch_count(void) { return g_launches.load(); }
 
+// Symmetric Hamming window of `chunk` samples in float64 rounded to float32 (chunking.py:24-28), made
+// and uploaded once per (device, length) and kept for the life of the process: a per-call upload of
+// megabytes from pageable memory would wait for the stream to drain (the staging buffers only empty
+// as the stream reaches the copy), which stalls the host behind a whole song of queued work.
+static int hamming_cached(int64_t chunk, const float** out) {
+  static std::mutex mu;
+  static std::map<std::pair<int, int64_t>, float*> cache;
+  int dev = 0;
+  TRC_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find({dev, chunk});
+  if (it != cache.end()) {
+    *out = it->second;
+    return TRC_OK;
+  }
+  std::vector<float> w((size_t)chunk);
+  if (chunk == 1) {
+    w[0] = 1.0f;
+  } else {
+    for (int64_t k = 0; k < chunk; ++k) w[k] = (float)(0.54 - 0.46 * std::cos(2.0 * M_PI * (double)k / (double)(chunk - 1)));
+  }
+  float* d = nullptr;
+  TRC_CUDA(cudaMalloc(&d, sizeof(float) * chunk));
+  TRC_CUDA(cudaMemcpy(d, w.data(), sizeof(float) * chunk, cudaMemcpyHostToDevice));
+  cache[{dev, chunk}] = d;
+  *out = d;
+  return TRC_OK;
+}
+
 int trc_ola(const float* d_chunks, int64_t chunk_out_len, const int64_t* h_starts, int n_chunks, int64_t chunk,
             int64_t n, float* d_result, void* stream) {
   if (!d_chunks || !h_starts || !d_result || n_chunks < 1 || chunk < 1 || n < 1 || chunk_out_len < 1 ||
@@ -941,24 +971,15 @@ int trc_ola(const float* d_chunks, int64_t chunk_out_len, const int64_t* h_start
     if (i && h_starts[i] <= h_starts[i - 1]) return fail(TRC_E_INVALID, "starts must be increasing");
   }
   cudaStream_t st = (cudaStream_t)stream;
-  // symmetric Hamming window in float64 rounded to float32 (chunking.py:24-28)
-  std::vector<float> w((size_t)chunk);
-  if (chunk == 1) {
-    w[0] = 1.0f;
-  } else {
-    for (int64_t k = 0; k < chunk; ++k) w[k] = (float)(0.54 - 0.46 * std::cos(2.0 * M_PI * (double)k / (double)(chunk - 1)));
-  }
-  float* d_w = nullptr;
+  const float* d_w = nullptr;
+  if (int rc = hamming_cached(chunk, &d_w)) return rc;
+  // the starts are a few hundred bytes: a pageable copy is staged at once and never waits on the stream
   int64_t* d_s = nullptr;
-  TRC_CUDA(cudaMallocAsync(&d_w, sizeof(float) * chunk, st));
   TRC_CUDA(cudaMallocAsync(&d_s, sizeof(int64_t) * n_chunks, st));
-  TRC_CUDA(cudaMemcpyAsync(d_w, w.data(), sizeof(float) * chunk, cudaMemcpyHostToDevice, st));
   TRC_CUDA(cudaMemcpyAsync(d_s, h_starts, sizeof(int64_t) * n_chunks, cudaMemcpyHostToDevice, st));
   trc::launch_chunk_ola(d_chunks, chunk_out_len, d_s, n_chunks, d_w, n, d_result, st);
   g_launches += 1;
   cudaError_t e = cudaGetLastError();
-  // pageable-source copies above are staged before returning, so the host vector may go out of scope
-  TRC_CUDA(cudaFreeAsync(d_w, st));
   TRC_CUDA(cudaFreeAsync(d_s, st));
   return check_launch(e, "overlap-add");
 }

@@ -13,8 +13,8 @@
 //   * The running row maximum is only raised when a tile's maximum exceeds it by more than 2^8 (then O
 //     and the row sum are rescaled in place); P <= 2^8 keeps 16-bit P exact enough and the final O / l
 //     is the exact softmax average.
-//   * The MMA issuer is an event loop over both tiles: it issues whichever product has its inputs
-//     ready (next S once the softmax has taken the previous one, P V once P is written).
+//   * Each query tile has its own MMA-issuing thread (warps 1 and 10), so the two tiles' products are
+//     issued independently: next S once the softmax has taken the previous one, P V once P is written.
 //   * Persistent CTAs walk the work items; Q is double buffered so the next item's first products
 //     start while the current item's epilogue runs.
 //
@@ -24,8 +24,8 @@
 //   freq mode (mode 1): sequences = (batch, frame, head), L = bands <= 64; a query tile holds two
 //                       sequences (block-diagonal mask), an item = four sequences, each tile has its own
 //                       single key tile.
-// Roles (320 threads): warp 0 TMA, warp 1 MMA issuer + TMEM owner, warps 2-5 softmax + epilogue of
-// tile A, warps 6-9 of tile B (thread = query row).
+// Roles (352 threads): warp 0 TMA, warp 1 MMA issuer of tile A + TMEM owner, warps 2-5 softmax +
+// epilogue of tile A, warps 6-9 of tile B (thread = query row), warp 10 MMA issuer of tile B.
 #pragma once
 
 #include "gemm.cuh"  // store32
@@ -33,7 +33,7 @@
 
 namespace trc {
 
-constexpr int kAttnThreads = 320;
+constexpr int kAttnThreads = 352;
 constexpr int kAttnKvStages = 3;
 
 struct AttnArgs {
@@ -94,7 +94,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   if (threadIdx.x == 0) {
     for (int b = 0; b < 2; ++b) {
       mbar_init(&q_full[b], 1);
-      mbar_init(&q_empty[b], 1);
+      mbar_init(&q_empty[b], 2);
       mbar_init(&s_full[b], 1);
       mbar_init(&s_free[b], 4);
       mbar_init(&p_full[b], 4);
@@ -103,9 +103,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
     for (int s = 0; s < kAttnKvStages; ++s) {
       mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+      mbar_init(&kv_empty[s], freq ? 1 : 2);  // time mode: both query tiles read every stage
     }
-    mbar_init(drain, 1);
+    mbar_init(drain, 2);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -179,95 +179,64 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         while (!mbar_try_wait(&q_full[k & 1], (uint32_t)(k >> 1) & 1) && global_ns() - t0 < kWaitLimitNs) {
         }
     }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------------ MMA issuer
+  } else if (warp == 1 || warp == kAttnThreads / 32 - 1) {
+    // ------------------------------------------------------------------ MMA issuers, one per query tile
     if (lane == 0) {
+      const int x = warp == 1 ? 0 : 1;
       const uint32_t idesc_qk = idesc_f16(128, 128, OperandType<TIn>::kFormat, 0, 0);
       const uint32_t idesc_pv = idesc_f16(128, 64, OperandType<TIn>::kFormat, 0, 1);  // V is MN-major
+      const uint32_t tS = tmem_base + tmem_col_s(x), tP = tmem_base + tmem_col_p(x),
+                     tO = tmem_base + tmem_col_o(x);
+      // shared-memory descriptors of stage 0 / Q buffer 0; other stages, buffers and K steps only move the
+      // 16-byte-unit start address in the low bits (every address is below 256 KB, so no carry)
+      const uint64_t q_desc0 = sdesc_sw128(smem_u32(smem + S::kQ + x * S::kTile), 16, 1024);
+      const uint64_t k_desc0 = sdesc_sw128(smem_u32(smem + S::kKV), 16, 1024);
+      const uint64_t v_desc0 = sdesc_sw128(smem_u32(smem + S::kKV + S::kTile), 8192, 1024);
+      constexpr uint32_t kStep = (2 * S::kTile) >> 4;  // one KV stage or one Q buffer
       int kvc = 0, local = 0;
-      uint32_t s_iss[2] = {0, 0};   // S tiles issued per query tile, all items (s_full / s_free phases)
-      uint32_t pv_iss[2] = {0, 0};  // P V products issued per query tile (p_full / p_free phases)
+      uint32_t g = 0;  // steps of this tile so far, all items (s_free / p_full / p_free phases)
       bool ok = true;
+      auto wait = [&](uint64_t* bar, uint32_t parity) {
+        if (ok && !mbar_wait(bar, parity, args.err, kErrWaitMma, abort_flag)) ok = false;
+        return ok;
+      };
+      // S(j) = Q K(j)^T into this tile's S columns
+      auto issue_s = [&](int j, uint64_t qd, int qb) {
+        const int idx = freq ? kvc + x : kvc + j;
+        const int st = idx % kAttnKvStages;
+        if (!wait(&kv_full[st], (uint32_t)(idx / kAttnKvStages) & 1)) return;
+        tc_fence_after();
+        const uint64_t kd = k_desc0 + (uint64_t)(st * kStep);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) mma_f16_ss(tS, qd + 2 * kk, kd + 2 * kk, idesc_qk, kk > 0 ? 1u : 0u);
+        mma_commit(&s_full[x]);
+        if (j == nsteps - 1) mma_commit(&q_empty[qb]);  // this tile's last read of the Q buffer
+      };
+      // O += P(j) V(j), P from TMEM
+      auto issue_pv = [&](int j) {
+        if (!wait(&p_full[x], g & 1u)) return;
+        if (j == 0 && local > 0 && !wait(&o_free[x], (uint32_t)(local - 1) & 1)) return;
+        tc_fence_after();
+        const int idx = freq ? kvc + x : kvc + j;
+        const int st = idx % kAttnKvStages;
+        const uint64_t vd = v_desc0 + (uint64_t)(st * kStep);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)  // 16 keys per MMA: P columns kk*8.., V rows kk*16..
+          mma_f16_ts(tO, tP + kk * 8, vd + kk * (2048 >> 4), idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(&p_free[x]);
+        mma_commit(&kv_empty[st]);  // one of the stage's readers (two in time mode)
+      };
       for (int item = blockIdx.x; item < args.num_items && ok; item += gridDim.x, ++local) {
         const int qb = local & 1;
-        if (!mbar_wait(&q_full[qb], (uint32_t)(local >> 1) & 1, args.err, kErrWaitMma, abort_flag)) {
-          ok = false;
-          break;
-        }
-        const uint32_t sq = smem_u32(smem + S::kQ + qb * 2 * S::kTile);
-        int s_next[2] = {0, 0}, p_next[2] = {0, 0};  // per tile: next S / next P V step of this item
-        uint64_t idle_since = 0;
-        uint32_t spins = 0;
-        while (p_next[0] < nsteps || p_next[1] < nsteps) {
-          bool progress = false;
-#pragma unroll
-          for (int x = 0; x < 2; ++x) {
-            // O += P V once the softmax has written P for this step
-            if (ok && p_next[x] < s_next[x] && mbar_test(&p_full[x], pv_iss[x] & 1u)) {
-              const int j = p_next[x];
-              if (j == 0 && local > 0 &&
-                  !mbar_wait(&o_free[x], (uint32_t)(local - 1) & 1, args.err, kErrWaitMma, abort_flag)) {
-                ok = false;
-              } else {
-                tc_fence_after();
-                const int idx = freq ? kvc + x : kvc + j;
-                const int st = idx % kAttnKvStages;
-                const uint32_t sv = smem_u32(smem + S::kKV + st * 2 * S::kTile + S::kTile);
-#pragma unroll
-                for (int kk = 0; kk < 8; ++kk) {  // 16 keys per MMA: P columns kk*8.., V rows kk*16..
-                  const uint64_t bd = sdesc_sw128(sv + kk * 2048, 8192, 1024);
-                  mma_f16_ts(tmem_base + tmem_col_o(x), tmem_base + tmem_col_p(x) + kk * 8, bd, idesc_pv,
-                             (j > 0 || kk > 0) ? 1u : 0u);
-                }
-                mma_commit(&p_free[x]);
-                // the stage's last reader: its own P V in freq mode, the later of the two tiles in time mode
-                if (freq || p_next[x ^ 1] > j) mma_commit(&kv_empty[st]);
-                ++p_next[x];
-                ++pv_iss[x];
-                progress = true;
-              }
-            }
-            // next S once the softmax has taken the previous one out of TMEM and its keys are loaded
-            if (ok && s_next[x] < nsteps && (s_iss[x] == 0 || mbar_test(&s_free[x], (s_iss[x] - 1) & 1u))) {
-              const int j = s_next[x];
-              const int idx = freq ? kvc + x : kvc + j;
-              const int st = idx % kAttnKvStages;
-              if (mbar_test(&kv_full[st], (uint32_t)(idx / kAttnKvStages) & 1)) {
-                tc_fence_after();
-                const uint32_t sk = smem_u32(smem + S::kKV + st * 2 * S::kTile);
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk) {
-                  const uint64_t ad = sdesc_sw128(sq + x * S::kTile + kk * 32, 16, 1024);
-                  const uint64_t bd = sdesc_sw128(sk + kk * 32, 16, 1024);
-                  mma_f16_ss(tmem_base + tmem_col_s(x), ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
-                }
-                mma_commit(&s_full[x]);
-                ++s_next[x];
-                ++s_iss[x];
-                if (s_next[0] == nsteps && s_next[1] == nsteps) mma_commit(&q_empty[qb]);  // Q read
-                progress = true;
-              }
-            }
-          }
-          if (!ok) break;
-          // bounded: no progress for kWaitLimitNs (or another role aborted) ends the kernel with an error
-          if (progress) {
-            idle_since = 0;
-          } else if ((++spins & 63u) == 0) {
-            if (*abort_flag) {
-              ok = false;
-              break;
-            }
-            const uint64_t now = global_ns();
-            if (idle_since == 0) {
-              idle_since = now;
-            } else if (now - idle_since > kWaitLimitNs) {
-              record_error(args.err, kErrWaitMma);
-              *abort_flag = 1;
-              ok = false;
-              break;
-            }
-          }
+        if (!wait(&q_full[qb], (uint32_t)(local >> 1) & 1)) break;
+        const uint64_t qd = q_desc0 + (uint64_t)(qb * kStep);
+        // the softmax must have taken the previous S out of TMEM before S(0) overwrites it
+        if (g > 0 && !wait(&s_free[x], (g - 1) & 1u)) break;
+        issue_s(0, qd, qb);
+        for (int j = 0; j < nsteps && ok; ++j, ++g) {
+          // S(j+1) as soon as the softmax has read S(j): it runs while the exponentials of step j are made
+          if (j + 1 < nsteps && wait(&s_free[x], g & 1u)) issue_s(j + 1, qd, qb);
+          issue_pv(j);
         }
         kvc += kv_per_item;
       }

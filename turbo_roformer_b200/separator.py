@@ -186,9 +186,12 @@ class Separator:
         gain = PEAK / peak if peak > PEAK else 1.0
         return np.ascontiguousarray(x * np.float32(gain) if gain != 1.0 else x), gain
 
-    def separate_device(self, x: torch.Tensor, overlap: float = 2.0, progress=None) -> torch.Tensor:
-        """(2, n) float32 already on the model's GPU (padded and gain-applied) -> (2, n) on the GPU."""
-        return overlap_add_cuda(self.net, x, self.chunk, overlap, batch=self.batch, progress=progress)
+    def separate_device(self, x: torch.Tensor, overlap: float = 2.0, progress=None, check: bool = True) -> torch.Tensor:
+        """(2, n) float32 already on the model's GPU (padded and gain-applied) -> (2, n) on the GPU.
+
+        With ``check=False`` the call only queues work (no host synchronisation); ``self.net.check()``
+        later synchronises and raises any device-side error."""
+        return overlap_add_cuda(self.net, x, self.chunk, overlap, batch=self.batch, progress=progress, check=check)
 
     @torch.inference_mode()
     def _separate_44k(self, x: np.ndarray, overlap: float, progress) -> np.ndarray:
@@ -202,9 +205,10 @@ class Separator:
         finite = torch.isfinite(peak)  # max|x| is finite iff every sample is (NaN propagates through amax)
         gain = torch.where(peak > PEAK, (PEAK / peak.double()).float(), torch.ones((), device=xd.device))
         xd.mul_(gain)
-        inst = self.separate_device(xd, overlap, progress)
+        inst = self.separate_device(xd, overlap, progress, check=False)
         inst.div_(gain)
         out = inst.cpu()
+        self.net.check()
         if not bool(finite):
             raise ValueError("input contains NaN or inf samples")
         return np.ascontiguousarray(out.numpy()[:, :n0])
