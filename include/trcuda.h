@@ -79,6 +79,13 @@ int64_t trc_output_length(const trc_handle* h, int64_t samples);
  * since the last check (the error word is then cleared). */
 int trc_check(trc_handle* h, void* stream);
 
+/* Non-blocking form of trc_check for callers that keep several forwards queued: enqueues on `stream` a
+ * copy of the handle's device error word into *host_word (pinned host memory; valid once the stream
+ * has passed this point) and then clears the device word. *host_word != 0 means a kernel queued
+ * before this call on the handle recorded an error. No reference counterpart (its forward is
+ * synchronous); used by Separator.submit. */
+int trc_error_async(trc_handle* h, int* host_word, void* stream);
+
 /* Replaces chunking.overlap_add's accumulation (turbo_roformer/chunking.py:54-61): Hamming-weighted
  * sum of chunk outputs, divided by the summed weights (clamped at 1e-10), in start order.
  * d_chunks [n_chunks][2][chunk_out_len]; h_starts: n_chunks increasing host int64 starts; chunk = C

@@ -129,3 +129,25 @@ def test_vocals_identity(sep):
     mix = S.chunk_audio(3 * SR, seed=9)
     inst = sep.separate(mix)
     np.testing.assert_allclose(inst + (mix - inst), mix, atol=1e-6)
+
+
+def test_submit_queues_songs_and_matches_separate(sep):
+    songs = [S.chunk_audio(SR * 3 + 77 * k, seed=10 + k) for k in range(3)]
+    ref = [sep.separate(m) for m in songs]
+    pinned = torch.from_numpy(songs[0]).pin_memory()
+    jobs = [sep.submit(pinned)] + [sep.submit(m) for m in songs[1:]]
+    # results in reverse order: each job owns its buffers
+    got = [j.result() for j in reversed(jobs)][::-1]
+    for r, g in zip(ref, got):
+        np.testing.assert_array_equal(r, g)
+    assert all(j.done() for j in jobs)
+    out = torch.empty(2, songs[1].shape[1], dtype=torch.float32).pin_memory()
+    np.testing.assert_array_equal(sep.submit(songs[1], out=out).result(), ref[1])
+    with pytest.raises(ValueError):
+        sep.submit(songs[1], out=torch.empty(2, 5, dtype=torch.float32).pin_memory())
+    bad = songs[2].copy()
+    bad[0, 99] = np.nan
+    job = sep.submit(bad)
+    with pytest.raises(ValueError):
+        job.result()
+    np.testing.assert_array_equal(sep.submit(songs[2]).result(), ref[2])  # the handle stays usable

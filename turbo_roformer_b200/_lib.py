@@ -18,6 +18,7 @@ _lib: ctypes.CDLL | None = None
 
 TRC_PREC_FP16 = 0
 TRC_PREC_BF16 = 1
+TRC_E_DEVICE = -3  # a kernel reported a device-side error (include/trcuda.h)
 
 c_int = ctypes.c_int
 c_i64 = ctypes.c_int64
@@ -64,6 +65,7 @@ SIGNATURES = {
     "trc_forward": (c_int, [c_vp, c_vp, c_int, c_i64, c_vp, c_vp]),
     "trc_output_length": (c_i64, [c_vp, c_i64]),
     "trc_check": (c_int, [c_vp, c_vp]),
+    "trc_error_async": (c_int, [c_vp, c_vp, c_vp]),
     "trc_ola": (c_int, [c_vp, c_i64, c_vp, c_int, c_i64, c_i64, c_vp, c_vp]),
     "trc_last_error": (c_char_p, []),
     "trc_ola_noalloc": (c_int, [c_vp, c_i64, c_vp, c_int, c_i64, c_i64, c_vp, c_vp]),

@@ -120,6 +120,14 @@ class CudaBSRoformer:
         """Synchronise the current stream and raise if a kernel reported a device-side error."""
         _lib.check(self.lib.trc_check(self.handle, ctypes.c_void_p(self.stream_ptr())))
 
+    def error_async(self, host_word: torch.Tensor) -> None:
+        """Queue a copy of the device error word into ``host_word`` (pinned int32, 1 element) on the
+        current stream and clear the device word; read it after the stream has passed this point."""
+        if host_word.dtype != torch.int32 or host_word.device.type != "cpu" or not host_word.is_pinned():
+            raise ValueError("host_word must be a pinned int32 CPU tensor")
+        _lib.check(self.lib.trc_error_async(self.handle, ctypes.c_void_p(host_word.data_ptr()),
+                                            ctypes.c_void_p(self.stream_ptr())))
+
     # ------------------------------------------------------------------ forward
     def forward_device(self, audio: torch.Tensor, out: torch.Tensor | None = None, check: bool = True) -> torch.Tensor:
         """audio (B, 2, L) float32 on this GPU -> (B, 2, hop * (L // hop)) on this GPU (current stream)."""

@@ -70,8 +70,11 @@ EncodeFn encode_fn() {
   return fn;
 }
 
-// Row-major 16-bit tensor: dims[0] innermost (elements), strides in bytes for dims[1..rank-1].
-// 128-byte swizzle, zero fill for out-of-range rows.
+// Element type code of make_map beyond TRC_PREC_FP16 / TRC_PREC_BF16.
+constexpr int kMapF32 = 2;
+
+// Row-major tensor of 16-bit (precision = TRC_PREC_*) or fp32 (kMapF32) elements: dims[0] innermost
+// (elements), strides in bytes for dims[1..rank-1]. 128-byte swizzle, zero fill for out-of-range rows.
 int make_map(CUtensorMap* m, int precision, const void* ptr, int rank, const uint64_t* dims,
              const uint64_t* strides_bytes, const uint32_t* box) {
   EncodeFn fn = encode_fn();
@@ -87,8 +90,9 @@ int make_map(CUtensorMap* m, int precision, const void* ptr, int rank, const uin
     es[i] = 1;
   }
   for (int i = 0; i < rank - 1; ++i) gs[i] = strides_bytes[i];
-  const CUtensorMapDataType dt =
-      precision == TRC_PREC_FP16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const CUtensorMapDataType dt = precision == kMapF32         ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : precision == TRC_PREC_FP16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                              : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   CUresult r = fn(m, dt, (cuuint32_t)rank, const_cast<void*>(ptr), gd, gs, bd, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(TRC_E_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
@@ -97,7 +101,7 @@ int make_map(CUtensorMap* m, int precision, const void* ptr, int rank, const uin
 
 // Cached variant for the forward path (keyed on everything that defines the map).
 int make_map_cached(trc_handle* h, CUtensorMap* m, const void* ptr, int rank, const uint64_t* dims,
-                    const uint64_t* strides_bytes, const uint32_t* box);
+                    const uint64_t* strides_bytes, const uint32_t* box, int dtype = -1);
 
 // [rows][cols] with box (64, box_rows)
 int map_2d(CUtensorMap* m, int prec, const void* p, uint64_t cols, uint64_t rows, uint32_t box_rows) {
@@ -266,11 +270,12 @@ struct Section {
 };
 
 int make_map_cached(trc_handle* h, CUtensorMap* m, const void* ptr, int rank, const uint64_t* dims,
-                    const uint64_t* strides_bytes, const uint32_t* box) {
+                    const uint64_t* strides_bytes, const uint32_t* box, int dtype) {
+  if (dtype < 0) dtype = h->prec;
   std::vector<uint64_t> key;
   key.reserve(16);
   key.push_back(reinterpret_cast<uint64_t>(ptr));
-  key.push_back((uint64_t)h->prec);
+  key.push_back((uint64_t)dtype);
   key.push_back((uint64_t)rank);
   for (int i = 0; i < rank; ++i) key.push_back(dims[i]);
   for (int i = 0; i < rank - 1; ++i) key.push_back(strides_bytes[i]);
@@ -280,7 +285,7 @@ int make_map_cached(trc_handle* h, CUtensorMap* m, const void* ptr, int rank, co
     *m = it->second;
     return TRC_OK;
   }
-  const int rc = make_map(m, h->prec, ptr, rank, dims, strides_bytes, box);
+  const int rc = make_map(m, dtype, ptr, rank, dims, strides_bytes, box);
   if (rc == TRC_OK) {
     if (h->map_cache.size() > 4096) h->map_cache.clear();
     h->map_cache[key] = *m;
@@ -489,7 +494,14 @@ int run_res_norm(trc_handle* h, int layer, int which, const void* A, float* X, v
   a.out0 = X;
   a.out1 = xn;
   a.bias = which == 0 ? nullptr : lw.b2.p;
-  const CUtensorMap mo[3] = {ma, ma, ma};  // unused by this epilogue
+  // X (fp32) and xn (16-bit) move through TMA in boxes of 32 rows: 32 columns of X, 64 of xn
+  CUtensorMap mo[3];
+  const uint64_t dims[2] = {256, (uint64_t)rows};
+  const uint64_t st_x[1] = {256 * 4}, st_n[1] = {256 * 2};
+  const uint32_t box_x[2] = {32, 32}, box_n[2] = {64, 32};
+  if ((rc = make_map_cached(h, &mo[0], X, 2, dims, st_x, box_x, kMapF32))) return rc;
+  if ((rc = make_map_cached(h, &mo[1], xn, 2, dims, st_n, box_n))) return rc;
+  mo[2] = mo[1];
   return check_launch(
       trc::launch_gemm(trc::EPI_RESNORM, h->prec, ma, which == 0 ? lw.m_wo : lw.m_w2, mo, a, h->num_sms, st),
       "res-norm gemm");
@@ -819,6 +831,15 @@ int trc_check(trc_handle* h, void* stream) {
     TRC_CUDA(cudaMemset(h->err.p, 0, sizeof(int)));
     return fail(TRC_E_DEVICE, "device error %d reported by a kernel (bounded wait expired or bad arguments)", e);
   }
+  return TRC_OK;
+}
+
+int trc_error_async(trc_handle* h, int* host_word, void* stream) {
+  if (!h || !host_word) return fail(TRC_E_INVALID, "null handle or host word");
+  TRC_CUDA(cudaSetDevice(h->device));
+  cudaStream_t st = (cudaStream_t)stream;
+  TRC_CUDA(cudaMemcpyAsync(host_word, h->err.p, sizeof(int), cudaMemcpyDeviceToHost, st));
+  TRC_CUDA(cudaMemsetAsync(h->err.p, 0, sizeof(int), st));
   return TRC_OK;
 }
 

@@ -22,7 +22,7 @@ from typing import Any
 import numpy as np
 import torch
 
-from . import audio
+from . import _lib, audio
 from .backend import CudaBSRoformer
 from .chunking import chunk_starts, overlap_add_cuda, step_for
 from .config import RESURRECTION, infer_config
@@ -194,24 +194,63 @@ class Separator:
         return overlap_add_cuda(self.net, x, self.chunk, overlap, batch=self.batch, progress=progress, check=check)
 
     @torch.inference_mode()
-    def _separate_44k(self, x: np.ndarray, overlap: float, progress) -> np.ndarray:
-        """separator.py:186-200 with the peak gain and the NaN/inf scan on the device: the caller's samples
-        are copied to the GPU once (at DMA speed when they live in pinned memory), the gain
-        PEAK / max|x| (rounded from double to float32, as the host code computes it) multiplies the mix
-        and divides the instrumental there, and one device-to-host copy returns the result."""
+    def _submit_44k(self, x, overlap: float, progress, out: torch.Tensor | None) -> "SeparationJob":
+        """separator.py:186-200 queued on the GPU without a host synchronisation.
+
+        The samples are copied to the GPU once (from pinned memory: the caller's, or a pinned staging
+        copy of a numpy mix), the peak gain PEAK / max|x| (rounded from double to float32, as the host
+        code computes it) multiplies the mix and divides the instrumental on the device, the NaN/inf scan
+        is max|x| being finite (NaN propagates through the maximum), and one asynchronous copy returns
+        the instrumental into pinned host memory. ``x`` is (2, n) float32: numpy or a CPU tensor."""
         n0 = x.shape[1]
-        xd = torch.from_numpy(np.ascontiguousarray(self._pad_short(x))).to(self.device, non_blocking=True)
+        if isinstance(x, torch.Tensor) and x.is_pinned() and n0 >= self.chunk:
+            src = x
+        else:
+            xp = np.ascontiguousarray(self._pad_short(x.numpy() if isinstance(x, torch.Tensor) else x))
+            src = torch.empty(xp.shape, dtype=torch.float32, pin_memory=True)
+            src.numpy()[...] = xp
+        if out is None:
+            out = torch.empty((2, n0), dtype=torch.float32, pin_memory=True)
+        elif out.shape != (2, n0) or out.dtype != torch.float32 or not out.is_pinned() or not out.is_contiguous():
+            raise ValueError(f"out must be a contiguous pinned float32 CPU tensor of shape (2, {n0})")
+        flags = torch.zeros(2, dtype=torch.int32, pin_memory=True)  # [device error word, non-finite input]
+        xd = src.to(self.device, non_blocking=True)
         peak = xd.abs().amax()
-        finite = torch.isfinite(peak)  # max|x| is finite iff every sample is (NaN propagates through amax)
         gain = torch.where(peak > PEAK, (PEAK / peak.double()).float(), torch.ones((), device=xd.device))
         xd.mul_(gain)
         inst = self.separate_device(xd, overlap, progress, check=False)
         inst.div_(gain)
-        out = inst.cpu()
-        self.net.check()
-        if not bool(finite):
-            raise ValueError("input contains NaN or inf samples")
-        return np.ascontiguousarray(out.numpy()[:, :n0])
+        out.copy_(inst[:, :n0], non_blocking=True)
+        flags[1:].copy_((~torch.isfinite(peak)).to(torch.int32).reshape(1), non_blocking=True)
+        self.net.error_async(flags[:1])
+        done = torch.cuda.Event()
+        done.record(torch.cuda.current_stream(self.device))
+        return SeparationJob(self, out, flags, done, keep=(src, xd, inst))
+
+    def _separate_44k(self, x: np.ndarray, overlap: float, progress) -> np.ndarray:
+        return self._submit_44k(x, overlap, progress, None).result()
+
+    def submit(self, mix, overlap: float = 2.0, out: torch.Tensor | None = None) -> "SeparationJob":
+        """Queue one song on the GPU and return at once; ``job.result()`` waits for it.
+
+        Same input contract and result as ``separate`` for 44.1 kHz input (no resampling here). Several
+        songs may be queued back to back: the host never synchronises between them, so the GPU stays busy
+        while the host prepares the next song. A mix in pinned memory (a pinned CPU tensor) is copied by
+        DMA straight from the caller's buffer; ``out`` may supply a pinned (2, n) float32 result buffer.
+        A service streaming many songs through one Separator is the intended user (no reference
+        counterpart: the reference separates one song per call)."""
+        if not overlap >= 1.0:
+            raise ValueError("overlap must be >= 1")
+        if isinstance(mix, torch.Tensor):
+            if mix.device.type != "cpu" or mix.dtype != torch.float32 or mix.ndim != 2 or mix.shape[0] != 2:
+                raise ValueError("a tensor mix must be a (2, n) float32 CPU tensor")
+            if mix.shape[1] == 0:
+                raise ValueError("empty input")
+            x = mix.contiguous()
+        else:
+            x = audio.to_stereo(audio.as_channels_first(mix, finite=False))
+        with self._lock:
+            return self._submit_44k(x, float(overlap), None, out)
 
     def separate(
         self,
@@ -285,3 +324,26 @@ class Separator:
             backend=self.backend,
             precision=self.precision,
         )
+
+
+class SeparationJob:
+    """A song queued by ``Separator.submit``. ``result()`` waits for it and returns the instrumental."""
+
+    def __init__(self, sep: Separator, out: torch.Tensor, flags: torch.Tensor, done: torch.cuda.Event, keep):
+        self._sep, self._out, self._flags, self._done, self._keep = sep, out, flags, done, keep
+
+    def done(self) -> bool:
+        """True once the GPU has finished the song (non-blocking)."""
+        return self._done.query()
+
+    def result(self) -> np.ndarray:
+        """float32 (2, n) instrumental (a view of the pinned result buffer); raises ValueError on NaN/inf
+        input and TRCError if a kernel reported a device-side error."""
+        self._done.synchronize()
+        self._keep = None
+        err, nonfinite = (int(v) for v in self._flags.tolist())
+        if err:
+            raise _lib.TRCError(_lib.TRC_E_DEVICE, f"device error {err} reported by a kernel (bounded wait expired)")
+        if nonfinite:
+            raise ValueError("input contains NaN or inf samples")
+        return self._out.numpy()
