@@ -329,69 +329,136 @@ __device__ __forceinline__ void epi_qkv(const GemmArgs& a, const TileCoord& tc, 
 // coalesced 128-byte row segments with all 32 rows' loads in flight before any store. Per-lane partial
 // sums of squares are combined with a 31-shuffle transpose-reduce (row `lane` ends in lane `lane`),
 // then the two halves of each row meet in shared memory.
+// Residual add + RMS norm (EPI_RESNORM). Each epilogue warp owns 32 rows (its TMEM lane quarter) x 128
+// columns (its half) and two 4 KB shared-memory boxes of 32 x 32 fp32 (128-byte swizzle):
+//   * the warp's X boxes are loaded by TMA before the accumulator is ready (resnorm_prefetch);
+//   * pass 1, per 32 columns: X_new = X + acc + b (thread = row), written back in place into the box and
+//     into TMEM (over the accumulator), the box stored to X by TMA and reloaded with the chunk after next;
+//   * the two halves exchange their partial sums of squares through shared memory;
+//   * pass 2: xn = X_new / max(||X_new||, eps) from TMEM, 16-bit, 64 columns per box, stored by TMA.
+// Rows past M are zero-filled by the loads and clipped by the stores.
+constexpr int kResBoxBytes = 32 * 32 * 4;
+
+struct ResState {
+  uint8_t* box;    // this warp's two boxes
+  uint64_t* xbar;  // this warp's two load barriers
+  int pend[2];     // parity of the load in flight per box, -1 if none
+};
+
+__device__ __forceinline__ void resnorm_load(ResState& r, const CUtensorMap* map_x, int k, int col, int row0,
+                                             int parity) {
+  mbar_arrive_expect_tx(&r.xbar[k], kResBoxBytes);
+  tma_load_2d(r.box + k * kResBoxBytes, map_x, &r.xbar[k], col, row0);
+  r.pend[k] = parity;
+}
+
+// Issue the loads of the first two X chunks of a tile (lane 0 of each epilogue warp).
+__device__ __forceinline__ void resnorm_prefetch(const GemmArgs& a, const TileCoord& tc, const EpiCtx& e,
+                                                 ResState& r, const CUtensorMap* map_x) {
+  const int row0 = tc.m0 + e.quarter * 32;
+  if (e.lane == 0 && row0 < a.M) {  // a warp whose 32 rows all lie past M moves no data
+    bulk_wait_read<0>();  // the previous tile's stores from these boxes have read them
+    resnorm_load(r, map_x, 0, e.hf * 128, row0, 0);
+    resnorm_load(r, map_x, 1, e.hf * 128 + 32, row0, 0);
+  }
+}
+
+// Wait (bounded) for loads still in flight, so no copy lands after the CTA has exited.
+__device__ __forceinline__ void resnorm_drain(const EpiCtx& e, ResState& r) {
+  if (e.lane != 0) return;
+  const uint64_t t0 = global_ns();
+  for (int k = 0; k < 2; ++k)
+    if (r.pend[k] >= 0)
+      while (!mbar_try_wait(&r.xbar[k], (uint32_t)r.pend[k]) && global_ns() - t0 < kWaitLimitNs) {
+      }
+}
+
 template <int BN, typename TIn>
-__device__ __forceinline__ void epi_resnorm(const GemmArgs& a, const TileCoord& tc, EpiCtx& e, int local_tile) {
-  float* X = static_cast<float*>(a.out0);
-  TIn* xn = static_cast<TIn*>(a.out1);
+__device__ __forceinline__ bool epi_resnorm(const GemmArgs& a, const TileCoord& tc, EpiCtx& e, ResState& r,
+                                            const CUtensorMap* map_x, const CUtensorMap* map_xn, float* rs_base,
+                                            int local_tile, volatile int* abort_flag) {
+  static_assert(BN == 256, "the residual-norm epilogue covers whole 256-wide rows");
   const int lane = e.lane;
   const int row0 = tc.m0 + e.quarter * 32;
-  const int nrows = min(32, a.M - row0);  // rows of this warp that exist (may be <= 0)
-  float* stage = e.scratch + e.ewarp * (32 * 33);
-  float ps[32];
-#pragma unroll
-  for (int r = 0; r < 32; ++r) ps[r] = 0.f;
+  const int swz = lane & 7;
+  const bool live = row0 < a.M;  // a warp whose rows all lie past M only joins the barriers
+  float ss = 0.f;
+  bool ok = true;  // a failed wait skips the work; the decision is made collectively before bar 3
 #pragma unroll 1
-  for (int c = 0; c < BN / 64; ++c) {
-    const int col = e.hf * (BN / 2) + c * 32;
+  for (int c = 0; c < 4 && ok && live; ++c) {
+    const int k = c & 1;
+    const int col = e.hf * 128 + c * 32;
+    if (!mbar_wait_warp(&r.xbar[k], (uint32_t)(c >> 1), a.err, kErrWaitEpilogue, abort_flag)) {
+      ok = false;
+      break;
+    }
+    if (lane == 0) r.pend[k] = -1;
     float v[32];
     tmem_ld32(e.taddr + col, v);
+    uint8_t* rowp = r.box + k * kResBoxBytes + lane * 128;
 #pragma unroll
-    for (int i = 0; i < 32; ++i) stage[lane * 33 + i] = v[i];
-    __syncwarp();
-    const float b = a.bias ? a.bias[col + lane] : 0.f;
-    float* xr = X + ((size_t)row0 * 256 + col + lane);  // row r of this warp at xr[r * 256]
-    float x[32];
-#pragma unroll
-    for (int r = 0; r < 32; ++r) x[r] = r < nrows ? xr[r * 256] : 0.f;
-#pragma unroll
-    for (int r = 0; r < 32; ++r) {
-      x[r] += stage[r * 33 + lane] + b;
-      ps[r] = fmaf(x[r], x[r], ps[r]);
+    for (int j = 0; j < 8; ++j) {
+      const float4 x4 = *reinterpret_cast<const float4*>(rowp + ((j ^ swz) << 4));
+      float4 b4 = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (a.bias) b4 = __ldg(reinterpret_cast<const float4*>(a.bias + col) + j);
+      v[4 * j] += x4.x + b4.x;
+      v[4 * j + 1] += x4.y + b4.y;
+      v[4 * j + 2] += x4.z + b4.z;
+      v[4 * j + 3] += x4.w + b4.w;
     }
 #pragma unroll
-    for (int r = 0; r < 32; ++r)
-      if (r < nrows) xr[r * 256] = x[r];
+    for (int i = 0; i < 32; ++i) ss = fmaf(v[i], v[i], ss);
+    tmem_st32(e.taddr + col, v);  // X_new over the accumulator, read back by pass 2
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      *reinterpret_cast<float4*>(rowp + ((j ^ swz) << 4)) =
+          make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    fence_async_smem();
     __syncwarp();
-  }
-#pragma unroll
-  for (int o = 16; o >= 1; o >>= 1) {
-    const bool upper = (lane & o) != 0;
-#pragma unroll
-    for (int i = 0; i < o; ++i) {
-      const float send = upper ? ps[i] : ps[i + o];
-      const float keep = upper ? ps[i + o] : ps[i];
-      ps[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+    if (lane == 0) {
+      tma_store_2d(map_x, r.box + k * kResBoxBytes, col, row0);
+      bulk_commit();
+      if (c + 2 < 4) {
+        bulk_wait_read<0>();  // the store has read the box: reuse it for the chunk after next
+        resnorm_load(r, map_x, k, col + 64, row0, 1);
+      }
     }
   }
-  float* rs = e.scratch + kEpiWarps * 32 * 33 + (local_tile & 1) * 256;
-  rs[e.hf * 128 + e.quarter * 32 + lane] = ps[0];
-  named_bar(3, 32 * kEpiWarps);
+  tmem_wait_st();
+  // the two column halves of a row exchange their sums of squares (double buffered across tiles)
+  float* rs = rs_base + (local_tile & 1) * 256;
+  rs[e.hf * 128 + e.quarter * 32 + lane] = ss;
+  if (!named_bar_and(3, 32 * kEpiWarps, ok)) return false;
   const float tot = rs[e.quarter * 32 + lane] + rs[128 + e.quarter * 32 + lane];
-  const float inv = 1.0f / fmaxf(sqrtf(tot), a.eps);  // for row row0 + lane
+  const float inv = 1.0f / fmaxf(sqrtf(tot), a.eps);
+  if (!live) return true;
+  if (lane == 0) bulk_wait_read<0>();  // both boxes free for the 16-bit output
+  __syncwarp();
 #pragma unroll 1
-  for (int c = 0; c < BN / 64; ++c) {
-    const int col = e.hf * (BN / 2) + c * 32;
-    const float* xr = X + ((size_t)row0 * 256 + col + lane);
-    TIn* nr = xn + ((size_t)row0 * 256 + col + lane);
-    float x[32];
+  for (int k = 0; k < 2; ++k) {
+    uint8_t* rowp = r.box + k * kResBoxBytes + lane * 128;
 #pragma unroll
-    for (int r = 0; r < 32; ++r) x[r] = r < nrows ? xr[r * 256] : 0.f;
+    for (int h = 0; h < 2; ++h) {
+      float v[32];
+      tmem_ld32(e.taddr + e.hf * 128 + (2 * k + h) * 32, v);
 #pragma unroll
-    for (int r = 0; r < 32; ++r) {
-      const float iv = __shfl_sync(0xffffffffu, inv, r);
-      if (r < nrows) nr[r * 256] = OperandType<TIn>::from_float(x[r] * iv);
+      for (int t = 0; t < 4; ++t) {
+        uint4 q;
+        q.x = OperandType<TIn>::pack2(v[8 * t] * inv, v[8 * t + 1] * inv);
+        q.y = OperandType<TIn>::pack2(v[8 * t + 2] * inv, v[8 * t + 3] * inv);
+        q.z = OperandType<TIn>::pack2(v[8 * t + 4] * inv, v[8 * t + 5] * inv);
+        q.w = OperandType<TIn>::pack2(v[8 * t + 6] * inv, v[8 * t + 7] * inv);
+        *reinterpret_cast<uint4*>(rowp + (((h * 4 + t) ^ swz) << 4)) = q;
+      }
+    }
+    fence_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(map_xn, r.box + k * kResBoxBytes, e.hf * 128 + k * 64, row0);
+      bulk_commit();
     }
   }
+  return true;
 }
 
 // GELU (dense) or tanh (grouped mask layer 1) on acc + bias, stored as 16-bit through TMA.
@@ -477,9 +544,10 @@ struct GemmSmem {
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kOutOffset = STAGES * kStageBytes;  // 4 staging slabs / residual-norm scratch
   static constexpr int kOutBytes = 4 * kSlabBytes;
-  static_assert(kEpiWarps * 32 * 33 * 4 + 2 * 256 * 4 <= kOutBytes, "residual-norm scratch must fit");
+  static_assert(kEpiWarps * 2 * kResBoxBytes <= kOutBytes, "residual-norm boxes must fit");
   static constexpr int kTabOffset = kOutOffset + kOutBytes;  // rotary rows (qkv only)
-  static constexpr int kBarOffset = kTabOffset + (EPI == EPI_QKV ? kTabBytes : 0);
+  static constexpr int kRsOffset = kTabOffset + (EPI == EPI_QKV ? kTabBytes : 0);  // row sums (res-norm only)
+  static constexpr int kBarOffset = kRsOffset + (EPI == EPI_RESNORM ? 2 * 256 * 4 : 0);
   static constexpr int kBytes = kBarOffset + 256 + 1024;  // + barriers + alignment slack
 };
 
@@ -498,6 +566,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* drain = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint64_t* xbars = drain + 2;  // residual-norm X loads: [epilogue warp][2]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -513,6 +582,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&acc_empty[b], 32 * kEpiWarps);
     }
     mbar_init(drain, 1);
+    if constexpr (EPI == EPI_RESNORM)
+      for (int b = 0; b < 2 * kEpiWarps; ++b) mbar_init(&xbars[b], 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -629,11 +700,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     e.scratch = reinterpret_cast<float*>(smem + S::kOutOffset);
     e.tab = reinterpret_cast<float*>(smem + S::kTabOffset);
     e.slot = 0;
+    ResState rst;
+    rst.box = smem + S::kOutOffset + e.ewarp * 2 * kResBoxBytes;
+    rst.xbar = xbars + e.ewarp * 2;
+    rst.pend[0] = rst.pend[1] = -1;
     int local = 0;
     for (int tile = blockIdx.x; tile < args.num_tiles; tile += gridDim.x, ++local) {
       const TileCoord tc = gemm_decode<BN>(args, tile);
       const int buf = local & 1;
       const uint32_t use = (uint32_t)(local >> 1);
+      if constexpr (EPI == EPI_RESNORM) resnorm_prefetch(args, tc, e, rst, &map_o0);  // overlaps this tile's MMAs
       if constexpr (EPI == EPI_QKV) {
         if (tc.n0 < 1024) {  // q or k tile: stage its rotary rows (overlaps this tile's MMAs)
           named_bar(3, 32 * kEpiWarps);  // every warp is done with the previous table
@@ -649,7 +725,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if constexpr (EPI == EPI_QKV) {
         epi_qkv<BN, TIn>(args, tc, e, &map_o0, &map_o1, &map_o2);
       } else if constexpr (EPI == EPI_RESNORM) {
-        epi_resnorm<BN, TIn>(args, tc, e, local);
+        const bool ok2 = epi_resnorm<BN, TIn>(args, tc, e, rst, &map_o0, &map_o1,
+                                              reinterpret_cast<float*>(smem + S::kRsOffset), local, abort_flag);
+        if (!named_bar_and(4, 32 * kEpiWarps, ok2)) break;
       } else if constexpr (EPI == EPI_GELU) {
         epi_act<BN, TIn>(args, tc, e, &map_o0, false);
       } else if constexpr (EPI == EPI_MASK_TANH) {
@@ -660,7 +738,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_before();
       mbar_arrive(&acc_empty[buf]);
     }
-    if (e.leader) bulk_wait<0>();  // this half's output stores have completed
+    if constexpr (EPI == EPI_RESNORM) {
+      resnorm_drain(e, rst);
+      if (lane == 0) bulk_wait<0>();  // this warp's stores have completed
+    } else {
+      if (e.leader) bulk_wait<0>();  // this half's output stores have completed
+    }
   }
 
   tc_fence_before();
