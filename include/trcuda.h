@@ -150,6 +150,19 @@ int trc_gemm_res_norm(trc_handle* h, int layer, int which, const void* d_A, floa
 /* kernels.cpp:610-642 gemm_gelu / fast.py:343-346: H = gelu(xn W1^T + b1), H [tokens][ff_inner]. */
 int trc_gemm_gelu(trc_handle* h, int layer, const void* d_xn, void* d_H, int64_t rows, void* stream);
 
+/* Replaces rope_pack (csrc/kernels.cpp:161-248, packed = false; the CPU-only VNNI packing has no GPU
+ * counterpart): d_qkvg [N][1544] 16-bit output of the unfused qkv+gate GEMM (gate logits include their
+ * bias) -> rotary q and k, plain v in the attention layout d_Q, d_K, d_V [seq][L][64] (16-bit) and
+ * d_G [N][8] = sigmoid(gate logits) fp32. mode 0 = time (L = T), 1 = freq (L = bands); N = batch*T*bands;
+ * the rotary angles are the model's (the handle's tables). */
+int trc_rope_pack(trc_handle* h, int mode, const void* d_qkvg, int batch, int T, void* d_Q, void* d_K, void* d_V,
+                  float* d_G, void* stream);
+
+/* Replaces gate_merge (csrc/kernels.cpp:391-408): d_O[token][h*64 + d] = d_G[token][h] * d_A[seq][pos][d]
+ * (16-bit in and out, product in fp32), the head merge of an attention computed elsewhere. */
+int trc_gate_merge(trc_handle* h, int mode, const void* d_A, const float* d_G, void* d_O, int batch, int T,
+                   void* stream);
+
 /* fast.py:370-376: audio [batch][2][samples] -> spectrum xin [batch][T][n_fft/2+1][2][2] fp32. */
 int trc_stft(trc_handle* h, const float* d_audio, int batch, int64_t samples, float* d_xin, void* stream);
 

@@ -223,6 +223,54 @@ def test_gemm_res_norm(tiny_cuda, tiny_cfg, tiny_sd, which):
     assert snr_db(xn_ref.numpy(), xn.float().cpu().numpy()) >= 55.0
 
 
+@pytest.mark.parametrize("mode", [0, 1])
+def test_rope_pack_matches_reference_semantics(tiny_cuda, tiny_cfg, tiny_sd, mode):
+    """rope_pack (kernels.cpp:161-248, unpacked): rotary in fp32 on the 16-bit GEMM output, one rounding."""
+    B, T = 2, 37
+    Fb = tiny_cfg.n_bands
+    N = B * T * Fb
+    g = torch.Generator().manual_seed(30 + mode)
+    qkvg = (torch.randn(N, 1544, generator=g) * 0.5).half()
+    x = qkvg.float()
+    freqs = tiny_sd[layer_prefix(mode) + "0.rotary_embed.freqs"]
+    q = R.rotate(to_sequences(x[:, :512], B, T, Fb, mode), freqs)
+    k = R.rotate(to_sequences(x[:, 512:1024], B, T, Fb, mode), freqs)
+    v = to_sequences(qkvg[:, 1024:1536], B, T, Fb, mode)
+    gates = torch.sigmoid(x[:, 1536:])
+    Q = torch.empty(N * 512, device="cuda", dtype=torch.float16)
+    K, V = torch.empty_like(Q), torch.empty_like(Q)
+    G = torch.empty(N, 8, device="cuda")
+    qd = qkvg.cuda()
+    call(tiny_cuda, "trc_rope_pack", mode, vp(qd), B, T, vp(Q), vp(K), vp(V), vp(G), stream(tiny_cuda))
+    # one fp32 rotation then one rounding: at most one 16-bit ulp from the rounded fp32 reference
+    for ref, got in ((q, Q), (k, K)):
+        got = got.view_as(ref).float().cpu()
+        ulp = torch.finfo(torch.float16).eps * ref.abs().clamp(min=2**-14)
+        assert ((got - ref).abs() <= ulp).all()
+    assert torch.equal(V.view_as(v).cpu(), v)  # v is moved, not recomputed
+    torch.testing.assert_close(G.cpu(), gates, rtol=2e-6, atol=2e-7)
+    with pytest.raises(Exception):
+        call(tiny_cuda, "trc_rope_pack", 2, vp(qd), B, T, vp(Q), vp(K), vp(V), vp(G), stream(tiny_cuda))
+
+
+@pytest.mark.parametrize("mode", [0, 1])
+def test_gate_merge_is_exact(tiny_cuda, tiny_cfg, mode):
+    """gate_merge (kernels.cpp:391-408): O = gate * A per head, one fp32 product rounded once."""
+    B, T = 2, 45
+    Fb = tiny_cfg.n_bands
+    N = B * T * Fb
+    g = torch.Generator().manual_seed(40 + mode)
+    L = T if mode == 0 else Fb
+    A = torch.randn(N * 8 // L, L, 64, generator=g).half()
+    G = torch.rand(N, 8, generator=g)
+    O = torch.empty(N, 512, device="cuda", dtype=torch.float16)
+    Ad, Gd = A.cuda(), G.cuda()
+    call(tiny_cuda, "trc_gate_merge", mode, vp(Ad), vp(Gd), vp(O), B, T, stream(tiny_cuda))
+    gate_seq = to_sequences(G.repeat_interleave(64, dim=1), B, T, Fb, mode)
+    ref = from_sequences((A.float() * gate_seq).half(), B, T, Fb, mode)
+    assert torch.equal(O.cpu(), ref)
+
+
 def test_gemm_gelu(tiny_cuda, tiny_cfg, tiny_sd):
     layer = 1
     N = 2 * 77 * tiny_cfg.n_bands

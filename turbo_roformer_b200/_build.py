@@ -17,7 +17,7 @@ CSRC = os.path.join(HERE, "csrc")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 LIB_NAME = "libtrcuda.so"
 LIB_PATH = os.path.join(HERE, LIB_NAME)
-SOURCES = ("api.cu", "tc.cu", "dsp.cu", "ola_noalloc.cu")
+SOURCES = ("api.cu", "tc.cu", "dsp.cu", "pack.cu", "ola_noalloc.cu")
 ARCH_FLAGS = ("-gencode", "arch=compute_100a,code=sm_100a")
 
 

@@ -1047,6 +1047,33 @@ int trc_gemm_gelu(trc_handle* h, int layer, const void* d_xn, void* d_H, int64_t
   return run_gelu(h, layer, d_xn, d_H, rows, (cudaStream_t)stream);
 }
 
+int trc_rope_pack(trc_handle* h, int mode, const void* d_qkvg, int batch, int T, void* d_Q, void* d_K, void* d_V,
+                  float* d_G, void* stream) {
+  TRC_REQUIRE_PREPARED(h);
+  if ((mode != 0 && mode != 1) || batch < 1 || T < 1 || !d_qkvg || !d_Q || !d_K || !d_V || !d_G)
+    return fail(TRC_E_INVALID, "bad rope_pack arguments");
+  const int64_t N = (int64_t)batch * T * h->nb;
+  if (N >= (1ll << 31)) return fail(TRC_E_INVALID, "too many tokens");
+  Tables* tab = get_tables(h, mode, mode == 0 ? T : h->nb);
+  if (!tab) return TRC_E_CUDA;
+  Section sec(h, "rope_pack", (cudaStream_t)stream);
+  trc::launch_rope_pack(h->prec, d_qkvg, tab->cos_t.p, tab->sin_t.p, mode, T, h->nb, N, d_Q, d_K, d_V, d_G,
+                        (cudaStream_t)stream);
+  return check_launch(cudaGetLastError(), "rope_pack");
+}
+
+int trc_gate_merge(trc_handle* h, int mode, const void* d_A, const float* d_G, void* d_O, int batch, int T,
+                   void* stream) {
+  TRC_REQUIRE_PREPARED(h);
+  if ((mode != 0 && mode != 1) || batch < 1 || T < 1 || !d_A || !d_G || !d_O)
+    return fail(TRC_E_INVALID, "bad gate_merge arguments");
+  const int64_t N = (int64_t)batch * T * h->nb;
+  if (N >= (1ll << 31)) return fail(TRC_E_INVALID, "too many tokens");
+  Section sec(h, "gate_merge", (cudaStream_t)stream);
+  trc::launch_gate_merge(h->prec, d_A, d_G, d_O, mode, T, h->nb, N, (cudaStream_t)stream);
+  return check_launch(cudaGetLastError(), "gate_merge");
+}
+
 int trc_stft(trc_handle* h, const float* d_audio, int batch, int64_t samples, float* d_xin, void* stream) {
   TRC_REQUIRE_PREPARED(h);
   if (batch < 1 || samples <= h->n_fft / 2) return fail(TRC_E_INVALID, "bad stft arguments");

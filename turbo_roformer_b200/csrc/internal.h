@@ -23,6 +23,12 @@ void launch_add_rmsnorm(float* X, const float* Y, void* out, int out_f32, int64_
 void launch_chunk_ola(const float* chunks, int64_t clen, const int64_t* d_starts, int n_chunks, const float* w,
                       int64_t n, float* out, cudaStream_t st);
 
+// pack.cu (unfused attention-layout helpers)
+void launch_rope_pack(int precision, const void* qkvg, const float* cos_tab, const float* sin_tab, int mode, int T,
+                      int F, int64_t N, void* Q, void* K, void* V, float* G, cudaStream_t st);
+void launch_gate_merge(int precision, const void* A, const float* G, void* O, int mode, int T, int F, int64_t N,
+                       cudaStream_t st);
+
 // tc.cu (tensor-core kernels). epi: EpiKind; precision: 0 fp16, 1 bf16; map_out: 3 output tensor maps
 // (unused ones may hold anything). Return cudaError_t of the launch.
 cudaError_t launch_gemm(int epi, int precision, const CUtensorMap& map_a, const CUtensorMap& map_b,
