@@ -178,6 +178,8 @@ def section_work(name: str, tokens_per_chunk: int, T: int, F: int) -> tuple[str,
         return "tensor", 2.0 * tokens_per_chunk * 512 * 256
     if name == "gemm_ff2_res_norm":
         return "tensor", 2.0 * tokens_per_chunk * 1024 * 256
+    if name == "ffn_res_norm":
+        return "tensor", 4.0 * tokens_per_chunk * 256 * 1024
     return None
 
 

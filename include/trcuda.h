@@ -150,6 +150,12 @@ int trc_gemm_res_norm(trc_handle* h, int layer, int which, const void* d_A, floa
 /* kernels.cpp:610-642 gemm_gelu / fast.py:343-346: H = gelu(xn W1^T + b1), H [tokens][ff_inner]. */
 int trc_gemm_gelu(trc_handle* h, int layer, const void* d_xn, void* d_H, int64_t rows, void* stream);
 
+/* The reference's feed-forward pair gemm_gelu + gemm_res_norm (csrc/kernels.cpp:610-642, :543-586;
+ * fast.py:320-333) in one kernel: d_X [rows][256] fp32 += GELU(d_xn W1^T + b1) W2^T + b2 and
+ * d_xn_out = X / max(|X|, 1e-12) (16-bit; may equal d_xn). The hidden activation stays on chip. */
+int trc_ffn_res_norm(trc_handle* h, int layer, const void* d_xn, float* d_X, void* d_xn_out, int64_t rows,
+                     void* stream);
+
 /* Replaces rope_pack (csrc/kernels.cpp:161-248, packed = false; the CPU-only VNNI packing has no GPU
  * counterpart): d_qkvg [N][1544] 16-bit output of the unfused qkv+gate GEMM (gate logits include their
  * bias) -> rotary q and k, plain v in the attention layout d_Q, d_K, d_V [seq][L][64] (16-bit) and

@@ -271,6 +271,29 @@ def test_gate_merge_is_exact(tiny_cuda, tiny_cfg, mode):
     assert torch.equal(O.cpu(), ref)
 
 
+@pytest.mark.parametrize("in_place", [False, True])
+def test_ffn_res_norm_fused(tiny_cuda, tiny_cfg, tiny_sd, in_place):
+    """Fused FF block == gemm_gelu then gemm_res_norm (kernels.cpp:610-642, :543-586) in fp32 math."""
+    layer = 3
+    B, T = 1, 91  # 2639 rows: a partial last 128-row block
+    N = B * T * tiny_cfg.n_bands
+    p = layer_prefix(layer)
+    g = torch.Generator().manual_seed(50 + int(in_place))
+    xn = F.normalize(torch.randn(N, 256, generator=g), dim=-1).half()
+    X = torch.randn(N, 256, generator=g)
+    gamma = tiny_sd[p + "1.net.0.gamma"]
+    W1 = tiny_sd[p + "1.net.1.weight"] * (gamma * 16.0)[None, :]
+    Hr = F.gelu(xn.float() @ W1.t() + tiny_sd[p + "1.net.1.bias"])
+    y = Hr @ tiny_sd[p + "1.net.4.weight"].t() + tiny_sd[p + "1.net.4.bias"]
+    Xr = X + y
+    xn_ref = F.normalize(Xr, dim=-1)
+    Xd, xd = X.cuda(), xn.cuda()
+    out = xd if in_place else torch.empty_like(xd)
+    call(tiny_cuda, "trc_ffn_res_norm", layer, vp(xd), vp(Xd), vp(out), N, stream(tiny_cuda))
+    assert snr_db(y.numpy(), (Xd.cpu() - X).numpy()) >= 50.0  # the added feed-forward term
+    assert snr_db(xn_ref.numpy(), out.float().cpu().numpy()) >= 55.0
+
+
 def test_gemm_gelu(tiny_cuda, tiny_cfg, tiny_sd):
     layer = 1
     N = 2 * 77 * tiny_cfg.n_bands

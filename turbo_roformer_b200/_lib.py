@@ -77,6 +77,7 @@ SIGNATURES = {
     "trc_attention": (c_int, [c_vp, c_int, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_vp]),
     "trc_gemm_res_norm": (c_int, [c_vp, c_int, c_int, c_vp, c_vp, c_vp, c_i64, c_vp]),
     "trc_gemm_gelu": (c_int, [c_vp, c_int, c_vp, c_vp, c_i64, c_vp]),
+    "trc_ffn_res_norm": (c_int, [c_vp, c_int, c_vp, c_vp, c_vp, c_i64, c_vp]),
     "trc_rope_pack": (c_int, [c_vp, c_int, c_vp, c_int, c_int, c_vp, c_vp, c_vp, c_vp, c_vp]),
     "trc_gate_merge": (c_int, [c_vp, c_int, c_vp, c_vp, c_vp, c_int, c_int, c_vp]),
     "trc_stft": (c_int, [c_vp, c_vp, c_int, c_i64, c_vp, c_vp]),

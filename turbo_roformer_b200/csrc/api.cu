@@ -20,6 +20,7 @@
 #include "attention.cuh"
 #include "gemm.cuh"
 #include "internal.h"
+#include "mlp.cuh"
 
 namespace {
 
@@ -161,6 +162,7 @@ struct LayerDev {
   DevBuf<uint16_t> w2;    // [256][ff]
   DevBuf<float> b2;       // [256]
   CUtensorMap m_wqkv, m_wo, m_w1, m_w2;
+  CUtensorMap m_w1c;  // W1 in 128-row boxes (hidden chunks of the fused feed-forward kernel)
 };
 
 struct Tables {
@@ -507,6 +509,30 @@ int run_res_norm(trc_handle* h, int layer, int which, const void* A, float* X, v
       "res-norm gemm");
 }
 
+// Fused feed-forward block: X += GELU(xn W1^T + b1) W2^T + b2, xn_out = X / max(|X|, 1e-12) (mlp.cuh).
+// xn_out may be xn itself: a row block's output is written after every read of that block's input.
+int run_ffn(trc_handle* h, int layer, const void* xn, float* X, void* xn_out, int64_t rows, cudaStream_t st) {
+  LayerDev& lw = *h->layers[layer];
+  if (h->ff % 128 || h->dim != 256) return fail(TRC_E_INVALID, "the fused feed-forward needs dim 256, hidden % 128 == 0");
+  CUtensorMap ma, mx, mxn;
+  int rc;
+  if ((rc = map_2d_cached(h, &ma, xn, 256, (uint64_t)rows, 128))) return rc;
+  const uint64_t dims[2] = {256, (uint64_t)rows};
+  const uint64_t st_x[1] = {256 * 4}, st_n[1] = {256 * 2};
+  const uint32_t box_x[2] = {32, 32}, box_n[2] = {64, 32};
+  if ((rc = make_map_cached(h, &mx, X, 2, dims, st_x, box_x, kMapF32))) return rc;
+  if ((rc = make_map_cached(h, &mxn, xn_out, 2, dims, st_n, box_n))) return rc;
+  trc::MlpArgs a;
+  a.num_blocks = (int)((rows + 127) / 128);
+  a.M = (int)rows;
+  a.n_chunks = h->ff / 128;
+  a.b1 = lw.b1.p;
+  a.b2 = lw.b2.p;
+  a.eps = 1e-12f;
+  a.err = h->err.p;
+  return check_launch(trc::launch_mlp(h->prec, ma, lw.m_w1c, lw.m_w2, mx, mxn, a, h->num_sms, st), "feed-forward");
+}
+
 int run_gelu(trc_handle* h, int layer, const void* xn, void* H, int64_t rows, cudaStream_t st) {
   LayerDev& lw = *h->layers[layer];
   CUtensorMap ma;
@@ -726,7 +752,8 @@ int trc_prepare(trc_handle* h) {
           (rc = L->b2.upload(*b2)))
         return rc;
       if ((rc = map_2d(&L->m_wqkv, prec, L->wqkv.p, d, 1544, 256)) || (rc = map_2d(&L->m_wo, prec, L->wo.p, 512, d, 256)) ||
-          (rc = map_2d(&L->m_w1, prec, L->w1.p, d, ff, 256)) || (rc = map_2d(&L->m_w2, prec, L->w2.p, ff, d, 256)))
+          (rc = map_2d(&L->m_w1, prec, L->w1.p, d, ff, 256)) || (rc = map_2d(&L->m_w2, prec, L->w2.p, ff, d, 256)) ||
+          (rc = map_2d(&L->m_w1c, prec, L->w1.p, d, ff, 128)))
         return rc;
       h->layers.push_back(std::move(L));
     }
@@ -888,12 +915,8 @@ int trc_forward(trc_handle* h, const float* d_audio, int batch, int64_t samples,
       if ((rc = run_res_norm(h, l, 0, h->O.p, h->X.p, h->xn.p, rows, st))) return rc;
     }
     {
-      Section sec(h, "gemm_ff1", st);
-      if ((rc = run_gelu(h, l, h->xn.p, h->H.p, rows, st))) return rc;
-    }
-    {
-      Section sec(h, "gemm_ff2_res_norm", st);
-      if ((rc = run_res_norm(h, l, 1, h->H.p, h->X.p, h->xn.p, rows, st))) return rc;
+      Section sec(h, "ffn_res_norm", st);
+      if ((rc = run_ffn(h, l, h->xn.p, h->X.p, h->xn.p, rows, st))) return rc;
     }
   }
   {
@@ -1038,6 +1061,15 @@ int trc_gemm_res_norm(trc_handle* h, int layer, int which, const void* d_A, floa
     return fail(TRC_E_INVALID, "bad gemm_res_norm arguments");
   Section sec(h, which == 0 ? "gemm_out_res_norm" : "gemm_ff2_res_norm", (cudaStream_t)stream);
   return run_res_norm(h, layer, which, d_A, d_X, d_xn, rows, (cudaStream_t)stream);
+}
+
+int trc_ffn_res_norm(trc_handle* h, int layer, const void* d_xn, float* d_X, void* d_xn_out, int64_t rows,
+                     void* stream) {
+  TRC_REQUIRE_PREPARED(h);
+  if (layer < 0 || layer >= 2 * h->depth || rows < 1 || !d_xn || !d_X || !d_xn_out)
+    return fail(TRC_E_INVALID, "bad ffn_res_norm arguments");
+  Section sec(h, "ffn_res_norm", (cudaStream_t)stream);
+  return run_ffn(h, layer, d_xn, d_X, d_xn_out, rows, (cudaStream_t)stream);
 }
 
 int trc_gemm_gelu(trc_handle* h, int layer, const void* d_xn, void* d_H, int64_t rows, void* stream) {

@@ -9,6 +9,7 @@ namespace trc {
 
 struct GemmArgs;
 struct AttnArgs;
+struct MlpArgs;
 
 // dsp.cu
 void launch_stft(const float* audio, int B, int64_t L, int T, int n, int hop, const float* window, const float2* tw,
@@ -33,6 +34,9 @@ void launch_gate_merge(int precision, const void* A, const float* G, void* O, in
 // (unused ones may hold anything). Return cudaError_t of the launch.
 cudaError_t launch_gemm(int epi, int precision, const CUtensorMap& map_a, const CUtensorMap& map_b,
                         const CUtensorMap* map_out, const GemmArgs& args, int num_sms, cudaStream_t st);
+cudaError_t launch_mlp(int precision, const CUtensorMap& ma, const CUtensorMap& mw1, const CUtensorMap& mw2,
+                       const CUtensorMap& mx, const CUtensorMap& mxn, const MlpArgs& args, int num_sms,
+                       cudaStream_t st);
 cudaError_t launch_attention(int precision, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                              const AttnArgs& args, int num_sms, cudaStream_t st);
 

@@ -4,6 +4,7 @@
 #include "attention.cuh"
 #include "gemm.cuh"
 #include "internal.h"
+#include "mlp.cuh"
 
 namespace trc {
 
@@ -73,6 +74,26 @@ cudaError_t launch_gemm(int epi, int precision, const CUtensorMap& ma, const CUt
                         const GemmArgs& args, int num_sms, cudaStream_t st) {
   return precision == 0 ? launch_gemm_p<__half>(epi, ma, mb, mo, args, num_sms, st)
                         : launch_gemm_p<__nv_bfloat16>(epi, ma, mb, mo, args, num_sms, st);
+}
+
+template <typename T>
+cudaError_t launch_mlp_t(const CUtensorMap& ma, const CUtensorMap& mw1, const CUtensorMap& mw2, const CUtensorMap& mx,
+                         const CUtensorMap& mxn, const MlpArgs& args, int num_sms, cudaStream_t st) {
+  auto kern = mlp_kernel<T>;
+  static std::atomic<unsigned long long> done{0};  // one per <T> instantiation
+  cudaError_t e = allow_smem(kern, MlpSmem::kBytes, done);
+  if (e != cudaSuccess) return e;
+  if (args.num_blocks <= 0) return cudaSuccess;
+  const int grid = args.num_blocks < num_sms ? args.num_blocks : num_sms;
+  kern<<<grid, kMlpThreads, MlpSmem::kBytes, st>>>(ma, mw1, mw2, mx, mxn, args);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_mlp(int precision, const CUtensorMap& ma, const CUtensorMap& mw1, const CUtensorMap& mw2,
+                       const CUtensorMap& mx, const CUtensorMap& mxn, const MlpArgs& args, int num_sms,
+                       cudaStream_t st) {
+  return precision == 0 ? launch_mlp_t<__half>(ma, mw1, mw2, mx, mxn, args, num_sms, st)
+                        : launch_mlp_t<__nv_bfloat16>(ma, mw1, mw2, mx, mxn, args, num_sms, st);
 }
 
 cudaError_t launch_attention(int precision, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
