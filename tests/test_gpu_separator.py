@@ -151,3 +151,12 @@ def test_submit_queues_songs_and_matches_separate(sep):
     with pytest.raises(ValueError):
         job.result()
     np.testing.assert_array_equal(sep.submit(songs[2]).result(), ref[2])  # the handle stays usable
+
+
+def test_service_load_overlap3(sep):
+    """Service-style load (several songs queued, overlap 3) equals one-at-a-time separation."""
+    songs = [S.chunk_audio(SR * 2 + 1000 * k, seed=60 + k) for k in range(4)]
+    ref = [sep.separate(m, overlap=3.0) for m in songs]
+    jobs = [sep.submit(torch.from_numpy(m).pin_memory(), overlap=3.0) for m in songs]
+    for r, j in zip(ref, jobs):
+        np.testing.assert_array_equal(j.result(), r)

@@ -206,20 +206,26 @@ struct EpiCtx {
   uint8_t* slabs;  // 4 staging slabs: [half][2]
   float* scratch;  // same memory, used by the residual-norm epilogue
   float* tab;      // rotary rows of the current q/k tile (qkv epilogue only)
-  int slot;        // next slab slot of this half (alternates 0, 1)
+  int slot;        // next slab slot of this half (alternates 0, 1 when slots == 2)
+  int slots;       // staging slabs per half: 2 (double buffered) or 1
 };
 
 // Before writing a slab: the store previously issued from it must have finished reading.
 __device__ __forceinline__ uint8_t* slab_acquire(EpiCtx& e) {
-  if (e.leader) bulk_wait_read<1>();
+  if (e.leader) {
+    if (e.slots == 2)
+      bulk_wait_read<1>();
+    else
+      bulk_wait_read<0>();
+  }
   named_bar(1 + e.hf, 128);
-  return e.slabs + (e.hf * 2 + e.slot) * kSlabBytes;
+  return e.slabs + (e.hf * e.slots + e.slot) * kSlabBytes;
 }
 // After writing: make the slab visible to the async proxy, then the leader stores it.
 __device__ __forceinline__ void slab_release(EpiCtx& e) {
   fence_async_smem();
   named_bar(1 + e.hf, 128);
-  e.slot ^= 1;
+  e.slot = e.slots == 2 ? e.slot ^ 1 : 0;
 }
 
 // ------------------------------------------------------------------------------------------------ epilogues
@@ -237,11 +243,13 @@ __device__ __forceinline__ bool qkv_token(const GemmArgs& a, const TileCoord& tc
 
 // Rotate 32 values (16 interleaved pairs (2j, 2j+1)) by the angles in cs[0..15], sn[0..15] (shared
 // memory, 16-byte aligned): x0 c - x1 s, x1 c + x0 s.
-__device__ __forceinline__ void rotate32(float (&v)[32], const float* cs, const float* sn) {
+// cs, sn: the thread's table rows (32 floats each, 16-byte chunks XOR-swizzled by swz = row & 7);
+// j0 = first chunk (0 for pairs 0..15, 4 for pairs 16..31).
+__device__ __forceinline__ void rotate32(float (&v)[32], const float* cs, const float* sn, int swz, int j0) {
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
-    const float4 c4 = reinterpret_cast<const float4*>(cs)[q];
-    const float4 s4 = reinterpret_cast<const float4*>(sn)[q];
+    const float4 c4 = reinterpret_cast<const float4*>(cs)[(j0 + q) ^ swz];
+    const float4 s4 = reinterpret_cast<const float4*>(sn)[(j0 + q) ^ swz];
     const float cc[4] = {c4.x, c4.y, c4.z, c4.w};
     const float ss[4] = {s4.x, s4.y, s4.z, s4.w};
 #pragma unroll
@@ -254,10 +262,11 @@ __device__ __forceinline__ void rotate32(float (&v)[32], const float* cs, const 
   }
 }
 
-// Rotary table rows of a q/k tile, staged in shared memory once per tile by all epilogue warps:
-// [cos|sin][row][kTabStride floats]; the stride of 36 floats keeps each thread's 16-byte reads of its
-// own row free of bank conflicts. time mode: rows = frames t0..t0+127; freq mode: rows = bands 0..63.
-constexpr int kTabStride = 36;
+// Rotary table rows of a row block, staged in shared memory by all epilogue warps: [cos|sin][row][32
+// floats], the 16-byte chunk j of row r stored at chunk j ^ (r & 7), so a warp reading chunk j of its
+// 32 rows touches every bank group (no conflicts). time mode: rows = frames t0..t0+127 (one load per
+// row block); freq mode: rows = bands 0..63 (the same for every block: one load per CTA).
+constexpr int kTabStride = 32;
 constexpr int kTabBytes = 2 * 128 * kTabStride * 4;
 
 __device__ __forceinline__ void load_rotary_rows(const GemmArgs& a, const TileCoord& tc, float* tab, int tid) {
@@ -271,7 +280,8 @@ __device__ __forceinline__ void load_rotary_rows(const GemmArgs& a, const TileCo
     const int row = rem >> 3, q = rem & 7;
     const int pos = min(pos0 + row, L - 1);
     const float* src = (table == 0 ? a.cos_tab : a.sin_tab) + (size_t)pos * 32 + q * 4;
-    *reinterpret_cast<float4*>(tab + (table * 128 + row) * kTabStride + q * 4) = __ldg(reinterpret_cast<const float4*>(src));
+    *reinterpret_cast<float4*>(tab + (table * 128 + row) * kTabStride + ((q ^ (row & 7)) * 4)) =
+        __ldg(reinterpret_cast<const float4*>(src));
   }
 }
 
@@ -298,8 +308,10 @@ __device__ __forceinline__ void epi_qkv(const GemmArgs& a, const TileCoord& tc, 
   const bool time = a.a_mode == A_TIME_SEQ;
   const int part = tc.n0 >> 9;  // 0 q, 1 k, 2 v
   const CUtensorMap* map = part == 0 ? mq : part == 1 ? mk : mv;
-  const float* cs = e.tab + (time ? r : (r & 63)) * kTabStride;
+  const int trow = time ? r : (r & 63);
+  const float* cs = e.tab + trow * kTabStride;
   const float* sn = cs + 128 * kTabStride;
+  const int swz = trow & 7;
 #pragma unroll 1
   for (int hh = 0; hh < 2; ++hh) {
     const int hc = e.hf * 2 + hh;                    // head within the tile
@@ -309,8 +321,8 @@ __device__ __forceinline__ void epi_qkv(const GemmArgs& a, const TileCoord& tc, 
     tmem_ld32(e.taddr + hc * 64, v0);
     tmem_ld32(e.taddr + hc * 64 + 32, v1);
     if (part < 2) {
-      rotate32(v0, cs, sn);
-      rotate32(v1, cs + 16, sn + 16);
+      rotate32(v0, cs, sn, swz, 0);
+      rotate32(v1, cs, sn, swz, 4);
     }
     stage_slab_row<TIn>(slab, r, v0, v1);
     slab_release(e);
@@ -539,16 +551,22 @@ __device__ __forceinline__ void epi_glu(const GemmArgs& a, const TileCoord& tc, 
 // ------------------------------------------------------------------------------------------------ kernel
 template <int BN, int STAGES, int EPI>
 struct GemmSmem {
+  // qkv keeps its A tile (K = 256) resident while it makes all N tiles of a row block, so only B streams
+  static constexpr bool kAStat = EPI == EPI_QKV;
   static constexpr int kABytes = kGemmBM * kGemmBK * 2;  // 16 KB
   static constexpr int kBBytes = BN * kGemmBK * 2;       // 32 KB at BN = 256
-  static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kOutOffset = STAGES * kStageBytes;  // 4 staging slabs / residual-norm scratch
-  static constexpr int kOutBytes = 4 * kSlabBytes;
-  static_assert(kEpiWarps * 2 * kResBoxBytes <= kOutBytes, "residual-norm boxes must fit");
+  static constexpr int kAResBytes = kAStat ? 4 * kABytes : 0;
+  static constexpr int kStageBytes = kAStat ? kBBytes : kABytes + kBBytes;
+  static constexpr int kStageOffset = kAResBytes;
+  static constexpr int kOutOffset = kStageOffset + STAGES * kStageBytes;  // staging slabs / residual-norm boxes
+  static constexpr int kSlabsPerHalf = kAStat ? 1 : 2;
+  static constexpr int kOutBytes = 2 * kSlabsPerHalf * kSlabBytes;
+  static_assert(EPI != EPI_RESNORM || kEpiWarps * 2 * kResBoxBytes <= kOutBytes, "residual-norm boxes must fit");
   static constexpr int kTabOffset = kOutOffset + kOutBytes;  // rotary rows (qkv only)
   static constexpr int kRsOffset = kTabOffset + (EPI == EPI_QKV ? kTabBytes : 0);  // row sums (res-norm only)
   static constexpr int kBarOffset = kRsOffset + (EPI == EPI_RESNORM ? 2 * 256 * 4 : 0);
   static constexpr int kBytes = kBarOffset + 256 + 1024;  // + barriers + alignment slack
+  static_assert(kBytes <= 232448, "shared memory per CTA");
 };
 
 template <int BN, int STAGES, int EPI, typename TIn>
@@ -567,6 +585,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   uint64_t* xbars = drain + 2;  // residual-norm X loads: [epilogue warp][2]
+  uint64_t* a_full = drain + 2;   // qkv: resident A tile loaded (same slots as xbars, another kernel)
+  uint64_t* a_empty = drain + 3;  // qkv: the MMAs of the row block have read the A tile
+  // qkv walks row blocks (groups of n_tiles consecutive tiles); other epilogues walk single tiles
+  const int n_units = S::kAStat ? args.num_tiles / args.n_tiles : args.num_tiles;
+  const int tiles_per_unit = S::kAStat ? args.n_tiles : 1;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -584,6 +607,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     mbar_init(drain, 1);
     if constexpr (EPI == EPI_RESNORM)
       for (int b = 0; b < 2 * kEpiWarps; ++b) mbar_init(&xbars[b], 1);
+    if constexpr (S::kAStat) {
+      mbar_init(a_full, 1);
+      mbar_init(a_empty, 1);
+    }
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -607,35 +634,68 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t phase = 0;
       int issued = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < args.num_tiles && ok; tile += gridDim.x) {
-        const TileCoord tc = gemm_decode<BN>(args, tile);
+      int lu = 0;       // units of this CTA so far (qkv: row blocks, a_full / a_empty phases)
+      int a_loads = 0;  // qkv: resident A tiles requested
+      for (int unit = blockIdx.x; unit < n_units && ok; unit += gridDim.x, ++lu) {
+        if constexpr (S::kAStat) {
+          // the resident A tile of this row block (all k blocks), once the previous block's MMAs read theirs
+          const TileCoord t0 = gemm_decode<BN>(args, unit * tiles_per_unit);
+          if (!mbar_wait(a_empty, ((uint32_t)lu & 1) ^ 1, args.err, kErrWaitProducer, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(a_full, args.k_blocks * S::kABytes);
+          ++a_loads;
+          for (int kb = 0; kb < args.k_blocks; ++kb) {
+            uint8_t* sa = smem + kb * S::kABytes;
+            const int kx = kb * kGemmBK;
+            if (a_dims == 2)
+              tma_load_2d(sa, &map_a, a_full, kx, t0.a1);
+            else if (a_dims == 3)
+              tma_load_3d(sa, &map_a, a_full, kx, t0.a1, t0.a2);
+            else
+              tma_load_4d(sa, &map_a, a_full, kx, t0.a1, t0.a2, t0.a3);
+          }
+        }
+        for (int u = 0; u < tiles_per_unit && ok; ++u) {
+        const TileCoord tc = gemm_decode<BN>(args, unit * tiles_per_unit + u);
         for (int kb = 0; kb < args.k_blocks; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, args.err, kErrWaitProducer, abort_flag)) {
             ok = false;
             break;
           }
-          uint8_t* sa = smem + stage * S::kStageBytes;
-          uint8_t* sb = sa + S::kABytes;
+          uint8_t* st = smem + S::kStageOffset + stage * S::kStageBytes;
           mbar_arrive_expect_tx(&full[stage], S::kStageBytes);
           const int kx = kb * kGemmBK;
-          if (a_dims == 2)
-            tma_load_2d(sa, &map_a, &full[stage], kx, tc.a1);
-          else if (a_dims == 3)
-            tma_load_3d(sa, &map_a, &full[stage], kx, tc.a1, tc.a2);
-          else
-            tma_load_4d(sa, &map_a, &full[stage], kx, tc.a1, tc.a2, tc.a3);
-          tma_load_2d(sb, &map_b, &full[stage], kx, tc.b_row);
+          if constexpr (S::kAStat) {
+            tma_load_2d(st, &map_b, &full[stage], kx, tc.b_row);
+          } else {
+            uint8_t* sb = st + S::kABytes;
+            if (a_dims == 2)
+              tma_load_2d(st, &map_a, &full[stage], kx, tc.a1);
+            else if (a_dims == 3)
+              tma_load_3d(st, &map_a, &full[stage], kx, tc.a1, tc.a2);
+            else
+              tma_load_4d(st, &map_a, &full[stage], kx, tc.a1, tc.a2, tc.a3);
+            tma_load_2d(sb, &map_b, &full[stage], kx, tc.b_row);
+          }
           ++issued;
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
           }
         }
+        }
       }
       if (!ok) {  // drain the copies still in flight before the CTA's shared memory is released
         for (int j = max(0, issued - STAGES); j < issued; ++j) {
           const uint64_t t0 = global_ns();
           while (!mbar_try_wait(&full[j % STAGES], (j / STAGES) & 1) && global_ns() - t0 < kWaitLimitNs) {
+          }
+        }
+        if (a_loads > 0) {
+          const uint64_t t0 = global_ns();
+          while (!mbar_try_wait(a_full, (uint32_t)(a_loads - 1) & 1) && global_ns() - t0 < kWaitLimitNs) {
           }
         }
       }
@@ -645,10 +705,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      int local = 0;
+      int local = 0, lu = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < args.num_tiles && ok; tile += gridDim.x, ++local) {
-        const TileCoord tc = gemm_decode<BN>(args, tile);
+      const uint32_t a_res = smem_u32(smem);  // qkv: resident A tile
+      for (int unit = blockIdx.x; unit < n_units && ok; unit += gridDim.x, ++lu) {
+        if constexpr (S::kAStat) {
+          if (!mbar_wait(a_full, (uint32_t)lu & 1, args.err, kErrWaitMma, abort_flag)) {
+            ok = false;
+            break;
+          }
+        }
+        for (int u = 0; u < tiles_per_unit && ok; ++u, ++local) {
+        const TileCoord tc = gemm_decode<BN>(args, unit * tiles_per_unit + u);
         const int buf = local & 1;
         const uint32_t use = (uint32_t)(local >> 1);
         if (!mbar_wait(&acc_empty[buf], (use & 1) ^ 1, args.err, kErrWaitMma, abort_flag)) {
@@ -664,8 +732,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t sa = smem_u32(smem + stage * S::kStageBytes);
-          const uint32_t sb = sa + S::kABytes;
+          const uint32_t st = smem_u32(smem + S::kStageOffset + stage * S::kStageBytes);
+          const uint32_t sa = S::kAStat ? a_res + kb * S::kABytes : st;
+          const uint32_t sb = S::kAStat ? st : st + S::kABytes;
 #pragma unroll
           for (int kk = 0; kk < kGemmBK / 16; ++kk) {
             const uint64_t ad = sdesc_sw128(sa + kk * 32, 16, 1024);
@@ -680,6 +749,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         if (!ok) break;
         mma_commit(&acc_full[buf]);
+        }
+        if constexpr (S::kAStat) mma_commit(a_empty);  // this row block's MMAs have read the A tile
       }
       // all MMAs issued by this thread are complete once `drain` fires
       mma_commit(drain);
@@ -700,18 +771,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     e.scratch = reinterpret_cast<float*>(smem + S::kOutOffset);
     e.tab = reinterpret_cast<float*>(smem + S::kTabOffset);
     e.slot = 0;
+    e.slots = S::kSlabsPerHalf;
     ResState rst;
     rst.box = smem + S::kOutOffset + e.ewarp * 2 * kResBoxBytes;
     rst.xbar = xbars + e.ewarp * 2;
     rst.pend[0] = rst.pend[1] = -1;
     int local = 0;
-    for (int tile = blockIdx.x; tile < args.num_tiles; tile += gridDim.x, ++local) {
-      const TileCoord tc = gemm_decode<BN>(args, tile);
+    bool run = true;
+    for (int unit = blockIdx.x; unit < n_units && run; unit += gridDim.x) {
+    for (int u = 0; u < tiles_per_unit; ++u, ++local) {
+      const TileCoord tc = gemm_decode<BN>(args, unit * tiles_per_unit + u);
       const int buf = local & 1;
       const uint32_t use = (uint32_t)(local >> 1);
       if constexpr (EPI == EPI_RESNORM) resnorm_prefetch(args, tc, e, rst, &map_o0);  // overlaps this tile's MMAs
       if constexpr (EPI == EPI_QKV) {
-        if (tc.n0 < 1024) {  // q or k tile: stage its rotary rows (overlaps this tile's MMAs)
+        // the row block's rotary rows, staged while its first tile's MMAs run: time mode once per row
+        // block (frames m0..m0+127), freq mode once per CTA (bands 0..63 for every block)
+        if (u == 0 && (args.a_mode == A_TIME_SEQ || local == 0)) {
           named_bar(3, 32 * kEpiWarps);  // every warp is done with the previous table
           load_rotary_rows(args, tc, e.tab, e.ewarp * 32 + lane);
           named_bar(3, 32 * kEpiWarps);
@@ -719,7 +795,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       // every epilogue warp takes the same decision, so no warp is left waiting at a named barrier
       const bool ok = mbar_wait_warp(&acc_full[buf], use & 1, args.err, kErrWaitEpilogue, abort_flag);
-      if (!named_bar_and(4, 32 * kEpiWarps, ok)) break;
+      if (!named_bar_and(4, 32 * kEpiWarps, ok)) {
+        run = false;
+        break;
+      }
       tc_fence_after();
       e.taddr = tmem_base + (uint32_t)(buf * BN) + ((uint32_t)(e.quarter * 32) << 16);
       if constexpr (EPI == EPI_QKV) {
@@ -727,7 +806,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       } else if constexpr (EPI == EPI_RESNORM) {
         const bool ok2 = epi_resnorm<BN, TIn>(args, tc, e, rst, &map_o0, &map_o1,
                                               reinterpret_cast<float*>(smem + S::kRsOffset), local, abort_flag);
-        if (!named_bar_and(4, 32 * kEpiWarps, ok2)) break;
+        if (!named_bar_and(4, 32 * kEpiWarps, ok2)) {
+          run = false;
+          break;
+        }
       } else if constexpr (EPI == EPI_GELU) {
         epi_act<BN, TIn>(args, tc, e, &map_o0, false);
       } else if constexpr (EPI == EPI_MASK_TANH) {
@@ -737,6 +819,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       tc_fence_before();
       mbar_arrive(&acc_empty[buf]);
+    }
     }
     if constexpr (EPI == EPI_RESNORM) {
       resnorm_drain(e, rst);
