@@ -41,14 +41,15 @@ UNIT = "audio-s/s"
 PUBLISHED = 1.38  # reference, 252.39 s song / 183.0 s wall on 8 Zen 4 cores (docs/benchmarks.md:71)
 
 # DRAM bytes (read + write) of one launch on ONE chunk (1700 frames x 62 bands = 105,400 tokens), from
-# `ncu --set full` on `bench.py --batch 1` (profiles/attention_kernel_chunk.md, profiles/gemm_kernel_chunk.md);
+# `ncu --set full` on `bench.py --batch 1` (profiles/attention_kernel_chunk.md, gemm_kernel_chunk.md,
+# mlp_kernel_chunk.md);
 # a batched launch moves this per chunk. None = not captured.
 TRAFFIC_PER_CHUNK = {
-    "attention_t": (328.19e6 + 87.67e6),
-    "attention_f": (327.61e6 + 82.77e6),
-    "qkv_rope_gemm": (55.33e6 + 268.42e6),
-    "gemm_out_res_norm": (216.23e6 + 106.42e6),
-    "gemm_ff1": (54.60e6 + 156.31e6),
+    "attention_t": (327.66e6 + 88.15e6),
+    "attention_f": (327.25e6 + 83.65e6),
+    "qkv_rope_gemm": (56.79e6 + 269.93e6),
+    "gemm_out_res_norm": (216.26e6 + 104.90e6),
+    "ffn_res_norm": (163.13e6 + 103.20e6),
 }
 
 
