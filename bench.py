@@ -41,9 +41,8 @@ UNIT = "audio-s/s"
 PUBLISHED = 1.38  # reference, 252.39 s song / 183.0 s wall on 8 Zen 4 cores (docs/benchmarks.md:71)
 
 # DRAM bytes (read + write) of one launch on ONE chunk (1700 frames x 62 bands = 105,400 tokens), from
-# `ncu --set full` on `bench.py --batch 1` (profiles/attention_kernel_chunk.md, gemm_kernel_chunk.md,
-# mlp_kernel_chunk.md);
-# a batched launch moves this per chunk. None = not captured.
+# `ncu --set full` on `bench.py --batch 1` (the one-chunk captures summarised under profiles/); a batched
+# launch moves this per chunk. None = not captured.
 TRAFFIC_PER_CHUNK = {
     "attention_t": (327.66e6 + 88.15e6),
     "attention_f": (327.25e6 + 83.65e6),
