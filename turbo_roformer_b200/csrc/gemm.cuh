@@ -559,7 +559,7 @@ struct GemmSmem {
   static constexpr int kStageBytes = kAStat ? kBBytes : kABytes + kBBytes;
   static constexpr int kStageOffset = kAResBytes;
   static constexpr int kOutOffset = kStageOffset + STAGES * kStageBytes;  // staging slabs / residual-norm boxes
-  static constexpr int kSlabsPerHalf = kAStat ? 1 : 2;
+  static constexpr int kSlabsPerHalf = 2;  // double-buffered staging slabs per column half
   static constexpr int kOutBytes = 2 * kSlabsPerHalf * kSlabBytes;
   static_assert(EPI != EPI_RESNORM || kEpiWarps * 2 * kResBoxBytes <= kOutBytes, "residual-norm boxes must fit");
   static constexpr int kTabOffset = kOutOffset + kOutBytes;  // rotary rows (qkv only)

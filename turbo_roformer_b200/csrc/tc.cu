@@ -30,7 +30,7 @@ constexpr int kStages = 3;
 template <int EPI, typename T>
 cudaError_t launch_gemm_t(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap* mo, const GemmArgs& args,
                           int num_sms, cudaStream_t st) {
-  constexpr int kSt = kStages;
+  constexpr int kSt = EPI == EPI_QKV ? 2 : kStages;  // qkv: resident A tile + rotary rows take the space
   using S = GemmSmem<kBN, kSt, EPI>;
   auto kern = gemm_kernel<kBN, kSt, EPI, T>;
   static std::atomic<unsigned long long> done{0};  // one per <EPI, T> instantiation
