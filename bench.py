@@ -211,7 +211,19 @@ def main() -> None:
     if world > 1:
         import datetime
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+        # NCCL prints a version banner on stdout while its communicator comes up; send that to stderr so
+        # stdout carries only rank 0's JSON line
+        sys.stdout.flush()
+        saved = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+            dist.barrier()
+            torch.cuda.synchronize()
+        finally:
+            sys.stdout.flush()
+            os.dup2(saved, 1)
+            os.close(saved)
 
     cfg = C.RESURRECTION
     sd = S.init_weights(cfg, seed=0)
@@ -229,7 +241,7 @@ def main() -> None:
 
     def step():
         if world > 1:
-            return separate_song_cuda(sep, x_dev, OVERLAP)
+            return separate_song_cuda(sep, x_dev, OVERLAP, check=False)
         return sep.separate_device(x_dev, OVERLAP, check=False)  # errors are checked after the timed region
 
     def barrier():

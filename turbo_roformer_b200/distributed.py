@@ -87,11 +87,14 @@ def ola_torch(chunks: torch.Tensor, starts: list[int], C: int, n: int) -> torch.
     return result.div_(weight.clamp_(min=1e-10))
 
 
-def separate_song_cuda(sep, x: torch.Tensor, overlap: float = 2.0, group=None) -> torch.Tensor | None:
+def separate_song_cuda(sep, x: torch.Tensor, overlap: float = 2.0, group=None,
+                       check: bool = True) -> torch.Tensor | None:
     """Shard one song over the process group with CUDA models.
 
     sep: a ``Separator`` (backend cuda) on this rank's GPU; x: (2, n) padded, gain-applied song on that GPU.
-    Returns the (2, n) instrumental on rank 0's GPU, None elsewhere.
+    Returns the (2, n) instrumental on rank 0's GPU, None elsewhere. ``check=False`` leaves the
+    device-error check (a stream synchronisation) to the caller (``sep.net.check()``), so the host can
+    queue the next song while the GPU works.
     """
     from .chunking import ola_device, run_chunks
 
@@ -99,7 +102,7 @@ def separate_song_cuda(sep, x: torch.Tensor, overlap: float = 2.0, group=None) -
     C = min(sep.chunk, x.shape[1])
 
     def run_shard(starts, out):
-        run_chunks(model, x, starts, C, sep.batch, out)
+        run_chunks(model, x, starts, C, sep.batch, out, check=check)
 
     return separate_sharded(run_shard, x.shape[1], sep.chunk, overlap, model.output_length(C), x.device,
                             lambda ch, st, c, n: ola_device(ch, st, c, n), group)
