@@ -86,6 +86,11 @@ int trc_check(trc_handle* h, void* stream);
  * synchronous); used by Separator.submit. */
 int trc_error_async(trc_handle* h, int* host_word, void* stream);
 
+/* Self-test of the device-side failure path: launches a kernel whose bounded wait on a barrier that
+ * nothing signals gives up after the wait limit (2 s) and records an error in the handle's error word,
+ * which the next trc_check reports as TRC_E_DEVICE. The context and the handle stay usable. */
+int trc_selftest_wait_timeout(trc_handle* h, void* stream);
+
 /* Replaces chunking.overlap_add's accumulation (turbo_roformer/chunking.py:54-61): Hamming-weighted
  * sum of chunk outputs, divided by the summed weights (clamped at 1e-10), in start order.
  * d_chunks [n_chunks][2][chunk_out_len]; h_starts: n_chunks increasing host int64 starts; chunk = C

@@ -7,6 +7,8 @@ model with these weights, tests/golden/golden_meta.json).
 
 from __future__ import annotations
 
+import ctypes
+
 import numpy as np
 import pytest
 import torch
@@ -22,7 +24,7 @@ pytestmark = pytest.mark.gpu
 @pytest.mark.parametrize("name,n,seed", [("chunk", 16256, 0), ("odd5000", 5000, 1), ("odd385", 385, 2)])
 def test_tiny_forward_matches_reference(tiny_cuda, golden_tiny, name, n, seed):
     x = torch.from_numpy(S.chunk_audio(n, seed=seed)).unsqueeze(0)
-    y = tiny_cuda(x)
+    y = tiny_cuda.forward(x)
     ref = golden_tiny[f"{name}_out"]
     assert y.shape == (1,) + ref.shape
     assert y.device.type == "cpu"
@@ -73,3 +75,18 @@ def test_full_chunk_matches_fp32_reference(full_cfg, full_sd, golden_full, cuda_
     # the oracle run here is the one pinned by the reference's own output
     assert snr_db(golden_full["excerpt"], ref[:, 300_000:304_096]) >= 100.0
     assert snr_db(ref, y) >= 50.0
+
+
+def test_bounded_wait_reports_and_recovers(tiny_cuda, tiny_cfg):
+    """A pipeline wait that can never complete ends with TRC_E_DEVICE after the wait limit, not a hang or
+    a fault, and the handle keeps working (the failure path of every pipelined kernel)."""
+    from turbo_roformer_b200 import _lib
+
+    st = ctypes.c_void_p(tiny_cuda.stream_ptr())
+    _lib.check(tiny_cuda.lib.trc_selftest_wait_timeout(tiny_cuda.handle, st))
+    with pytest.raises(_lib.TRCError, match="device error"):
+        tiny_cuda.check()
+    x = torch.from_numpy(S.chunk_audio(tiny_cfg.stft_hop_length * 40, seed=3)).unsqueeze(0)
+    y = tiny_cuda.forward(x)
+    tiny_cuda.check()
+    assert torch.isfinite(y).all()

@@ -66,6 +66,7 @@ SIGNATURES = {
     "trc_output_length": (c_i64, [c_vp, c_i64]),
     "trc_check": (c_int, [c_vp, c_vp]),
     "trc_error_async": (c_int, [c_vp, c_vp, c_vp]),
+    "trc_selftest_wait_timeout": (c_int, [c_vp, c_vp]),
     "trc_ola": (c_int, [c_vp, c_i64, c_vp, c_int, c_i64, c_i64, c_vp, c_vp]),
     "trc_last_error": (c_char_p, []),
     "trc_ola_noalloc": (c_int, [c_vp, c_i64, c_vp, c_int, c_i64, c_i64, c_vp, c_vp]),

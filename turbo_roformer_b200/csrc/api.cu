@@ -870,6 +870,13 @@ int trc_error_async(trc_handle* h, int* host_word, void* stream) {
   return TRC_OK;
 }
 
+int trc_selftest_wait_timeout(trc_handle* h, void* stream) {
+  if (!h) return fail(TRC_E_INVALID, "null handle");
+  TRC_CUDA(cudaSetDevice(h->device));
+  trc::launch_wait_timeout_selftest(h->err.p, (cudaStream_t)stream);
+  return check_launch(cudaGetLastError(), "wait-timeout self-test");
+}
+
 #define TRC_REQUIRE_PREPARED(h)                                               \
   do {                                                                        \
     if (!(h)) return fail(TRC_E_INVALID, "null handle");                      \

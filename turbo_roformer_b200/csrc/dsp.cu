@@ -319,6 +319,23 @@ void launch_add_rmsnorm(float* X, const float* Y, void* out, int out_f32, int64_
     add_rmsnorm_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(X, Y, out, out_f32, rows, eps);
 }
 
+// Self-test of the bounded-wait error path every pipelined kernel relies on: one thread waits on a
+// shared-memory barrier that nothing will signal; after the wait limit it records kErrWaitSelftest in
+// the error word and returns, leaving the context usable. No fault, no trap, no hang.
+__global__ void wait_timeout_selftest_kernel(int* err) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_wait(&bar, 0, err, kErrWaitSelftest, &abort_flag);
+}
+
+void launch_wait_timeout_selftest(int* err, cudaStream_t st) { wait_timeout_selftest_kernel<<<1, 32, 0, st>>>(err); }
+
 void launch_chunk_ola(const float* chunks, int64_t clen, const int64_t* d_starts, int n_chunks, const float* w,
                       int64_t n, float* out, cudaStream_t st) {
   chunk_ola_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(chunks, clen, d_starts, n_chunks, w, n, out);

@@ -21,6 +21,7 @@ void launch_band_split(const float* xin, int width, int rows, int nbands, const 
 void launch_rownorm(const float* X, void* xn, int64_t rows, float eps, int precision, cudaStream_t st);
 void launch_add_rmsnorm(float* X, const float* Y, void* out, int out_f32, int64_t rows, float eps, int precision,
                         cudaStream_t st);
+void launch_wait_timeout_selftest(int* err, cudaStream_t st);
 void launch_chunk_ola(const float* chunks, int64_t clen, const int64_t* d_starts, int n_chunks, const float* w,
                       int64_t n, float* out, cudaStream_t st);
 

@@ -22,6 +22,7 @@ enum DeviceError : int {
   kErrWaitSoftmax = 4,    // attention softmax gave up waiting for scores / PV
   kErrWaitDrain = 5,      // abort path gave up draining in-flight copies
   kErrBadArgs = 6,        // kernel-side argument check failed
+  kErrWaitSelftest = 7,   // the bounded-wait self-test gave up (expected: nothing signals its barrier)
 };
 
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s: pipeline waits are microseconds when healthy
