@@ -132,25 +132,28 @@ __global__ void istft_ola_kernel(const float* __restrict__ frames, int B, int T,
 // RMSNorm gain sqrt(din) * gamma folded into W'. One block = 64 rows (batch x frame) of one band;
 // thread o = output feature. wt [sum din][256] (transposed, folded), bias [nbands][256],
 // X [rows][nbands][256] fp32.
+// R rows (frames) x one band x 256 outputs per block: a thread owns one output column for R rows; small R
+// gives many short blocks, which balances the very different band widths (8 to 512 inputs) over the SMs.
+template <int R>
 __global__ void __launch_bounds__(256) band_split_kernel(const float* __restrict__ xin, int width, int rows,
                                                          int nbands, const int* __restrict__ band_off,
                                                          const float* __restrict__ wt, const float* __restrict__ bias,
                                                          float* __restrict__ X) {
-  __shared__ __align__(16) float xs[64][68];  // row stride 68 keeps float4 reads 16-byte aligned
-  __shared__ float ssq_s[64];
+  __shared__ __align__(16) float xs[R][68];  // row stride 68 keeps float4 reads 16-byte aligned
+  __shared__ float ssq_s[R];
   const int band = blockIdx.y;
-  const int r0 = blockIdx.x * 64;
+  const int r0 = blockIdx.x * R;
   const int off = band_off[band];
   const int din = band_off[band + 1] - off;  // 4 * bins: always a multiple of 4
   const int o = threadIdx.x;
-  float acc[64];
+  float acc[R];
 #pragma unroll
-  for (int r = 0; r < 64; ++r) acc[r] = 0.f;
+  for (int r = 0; r < R; ++r) acc[r] = 0.f;
   float ssq = 0.f;
   for (int c0 = 0; c0 < din; c0 += 64) {
     const int cw = min(64, din - c0);
 #pragma unroll 4
-    for (int k = 0; k < 16; ++k) {
+    for (int k = 0; k < R / 4; ++k) {
       const int e = o + k * 256;
       const int row = e >> 6, col = e & 63;
       float v = 0.f;
@@ -158,25 +161,25 @@ __global__ void __launch_bounds__(256) band_split_kernel(const float* __restrict
       xs[row][col] = v;
     }
     __syncthreads();
-    if (o < 64) {
+    if (o < R) {
       for (int col = 0; col < cw; ++col) ssq += xs[o][col] * xs[o][col];
     }
     for (int i = 0; i < cw; i += 4) {
       const float* wp = wt + (size_t)(off + c0 + i) * 256 + o;
       const float w0 = wp[0], w1 = wp[256], w2 = wp[512], w3 = wp[768];
 #pragma unroll
-      for (int r = 0; r < 64; ++r) {
+      for (int r = 0; r < R; ++r) {
         const float4 xv = *reinterpret_cast<const float4*>(&xs[r][i]);
         acc[r] = fmaf(xv.w, w3, fmaf(xv.z, w2, fmaf(xv.y, w1, fmaf(xv.x, w0, acc[r]))));
       }
     }
     __syncthreads();
   }
-  if (o < 64) ssq_s[o] = ssq;
+  if (o < R) ssq_s[o] = ssq;
   __syncthreads();
   const float bo = bias[band * 256 + o];
 #pragma unroll 4
-  for (int r = 0; r < 64; ++r) {
+  for (int r = 0; r < R; ++r) {
     const int row = r0 + r;
     if (row < rows) {
       const float inv = 1.0f / fmaxf(sqrtf(ssq_s[r]), 1e-12f);
@@ -298,8 +301,8 @@ void launch_istft(const float* xin, const float* mask, int B, int T, int n, int 
 
 void launch_band_split(const float* xin, int width, int rows, int nbands, const int* band_off, const float* wt,
                        const float* bias, float* X, cudaStream_t st) {
-  dim3 grid((rows + 63) / 64, nbands);
-  band_split_kernel<<<grid, 256, 0, st>>>(xin, width, rows, nbands, band_off, wt, bias, X);
+  dim3 grid((rows + 15) / 16, nbands);
+  band_split_kernel<16><<<grid, 256, 0, st>>>(xin, width, rows, nbands, band_off, wt, bias, X);
 }
 
 void launch_rownorm(const float* X, void* xn, int64_t rows, float eps, int precision, cudaStream_t st) {
