@@ -305,6 +305,10 @@ def main() -> None:
     torch.cuda.synchronize()
     if world == 1:
         outs = [torch.empty(2, n, dtype=torch.float32).pin_memory() for _ in range(args.steps)]
+        # untimed pass of the same queue: the caching allocator then holds the device buffers of
+        # args.steps songs in flight, so the timed pass makes no cudaMalloc calls
+        for j in [sep.submit(pinned, overlap=OVERLAP, out=outs[k]) for k in range(args.steps)]:
+            j.result()
         t0 = time.perf_counter()
         jobs = [sep.submit(pinned, overlap=OVERLAP, out=outs[k]) for k in range(args.steps)]
         results = [j.result() for j in jobs]

@@ -4,15 +4,16 @@
 // src/turbo_roformer/csrc/kernels.cpp:610-642 and :543-586, sequenced in fast.py:320-333) with one
 // kernel in which the hidden activation H never leaves the SM: per 128-row block the 1024 hidden units
 // are processed in chunks of 128,
-//   G1(c): acc1[c % 2] = xn_block W1[c]^T          (TMEM, 128 x 128, double buffered)
-//   GELU : H[c % 2] = gelu(acc1 + b1[c]) 16-bit     (shared memory, the A operand layout of G2)
-//   G2(c): acc2 += H[c % 2] W2[:, c]^T              (TMEM, 128 x 256, accumulated over the chunks)
+//   G1(c): acc1[c % 2] = xn_block W1[c]^T          (TMEM, 128 x 128 fp32, double buffered)
+//   GELU : H = gelu(acc1 + b1[c]) 16-bit, written back over the first half of each 64-column half of
+//          acc1[c % 2] (TMEM, the A operand of the next MMA)
+//   G2(c): acc2 += H W2[:, c]^T                     (TMEM, 128 x 256, accumulated over the chunks)
 // and the residual + norm epilogue of the finished block runs while the next block's chunks are made.
-// The GELU warps release an acc1 buffer as soon as they have loaded it, so G1(c + 2) runs on the tensor
-// core while GELU(c) computes: the MMA order per block is G1(0), G1(1), then G1(c + 2), G2(c) for
-// c = 0.., and the TMA producer streams the operands in exactly that order through one ring of 32 KB
-// stages (A + W1 k-blocks for G1, W2 k-blocks for G2). Rows past M are zero-filled by the loads and
-// clipped by the stores.
+// The 128 x 256 xn block is loaded once per block and stays in shared memory for its eight G1s, so the
+// ring of 32 KB stages streams weights only (two W1 k-blocks or one W2 k-block per stage), in the MMA
+// order G1(0), G1(1), then G2(c), G1(c + 2) for c = 0..: tcgen05 MMAs of one thread execute in issue
+// order, so G1(c + 2) overwrites acc1[c % 2] only after G2(c) has read the H stored there, while the
+// GELU warps work on the other buffer. Rows past M are zero-filled by the loads and clipped by the stores.
 //
 // Roles (448 threads): warp 0 TMA producer, warp 1 MMA issuer + TMEM owner, warps 2-9 GELU (lane
 // quarter warp % 4, 64 of the chunk's 128 columns each), warps 10-13 residual + norm (one lane quarter
@@ -44,14 +45,14 @@ struct MlpArgs {
 
 struct MlpSmem {
   static constexpr int kRing = 0;                                  // [stages][32 KB]
-  static constexpr int kH = kRing + kMlpStages * kMlpStageBytes;  // [2][2 k-blocks][128 rows x 64] 16-bit
-  static constexpr int kBox = kH + 2 * 32768;                      // [epilogue warp][2 boxes]
+  static constexpr int kA = kRing + kMlpStages * kMlpStageBytes;  // [4 k-blocks][128 rows x 64] 16-bit xn block
+  static constexpr int kBox = kA + 4 * 16384;                      // [epilogue warp][kMlpBoxes boxes]
   static constexpr int kBar = kBox + kMlpEpiWarps * kMlpBoxes * kMlpBoxBytes;
-  static constexpr int kBytes = kBar + 512 + 1024;  // barriers (33 x 8 B + TMEM slot + abort flag), alignment slack
+  static constexpr int kBytes = kBar + 512 + 1024;  // barriers (31 x 8 B + TMEM slot + abort flag), alignment slack
   static_assert(kBytes <= 232448, "shared memory per CTA");
 };
 
-// TMEM: acc1 buffers at columns 0 and 128, acc2 at 256..511.
+// TMEM: acc1 buffers at columns 0 and 128 (H of the chunk in columns +0..31 and +64..95), acc2 at 256..511.
 constexpr uint32_t kMlpAcc2 = 256;
 
 template <typename TIn>
@@ -65,10 +66,10 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kBar);
   uint64_t* empty = full + kMlpStages;
   uint64_t* a1_full = empty + kMlpStages;  // [2] G1 chunk in acc1 (MMA commit)
-  uint64_t* a1_empty = a1_full + 2;        // [2] acc1 buffer loaded by the GELU warps (one arrive each)
-  uint64_t* h_full = a1_empty + 2;         // [2] H chunk written (one arrive per GELU warp)
-  uint64_t* h_empty = h_full + 2;          // [2] G2 has read the H buffer (MMA commit)
-  uint64_t* a2_full = h_empty + 2;         // block's acc2 complete (MMA commit)
+  uint64_t* h_full = a1_full + 2;          // [2] H chunk written to TMEM (one arrive per GELU warp)
+  uint64_t* a_full = h_full + 2;           // xn block loaded (TMA bytes)
+  uint64_t* a_empty = a_full + 1;          // the block's last G1 has read the xn block (MMA commit)
+  uint64_t* a2_full = a_empty + 1;         // block's acc2 complete (MMA commit)
   uint64_t* a2_empty = a2_full + 1;        // epilogue done with acc2 (one arrive per epilogue warp)
   uint64_t* xbars = a2_empty + 1;          // [epilogue warp][kMlpBoxes] X box loads
   uint64_t* drain = xbars + kMlpBoxes * kMlpEpiWarps;
@@ -86,10 +87,10 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&a1_full[b], 1);
-      mbar_init(&a1_empty[b], kMlpGeluWarps);
       mbar_init(&h_full[b], kMlpGeluWarps);
-      mbar_init(&h_empty[b], 1);
     }
+    mbar_init(a_full, 1);
+    mbar_init(a_empty, 1);
     mbar_init(a2_full, 1);
     mbar_init(a2_empty, kMlpEpiWarps);
     for (int b = 0; b < kMlpBoxes * kMlpEpiWarps; ++b) mbar_init(&xbars[b], 1);
@@ -134,14 +135,23 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
           phase ^= 1;
         }
       };
+      int a_loads = 0;
       for (int blk = blockIdx.x; blk < args.num_blocks && ok; blk += gridDim.x) {
         const int m0 = blk * 128;
-        auto load_g1 = [&](int c) {  // 4 k-blocks: xn[m0.., k] (16 KB) + W1[c*128.., k] (16 KB)
-          for (int kb = 0; kb < 4 && ok; ++kb) {
+        // the xn block: once the previous block's last G1 has read the buffer
+        if (a_loads > 0 && !mbar_wait(a_empty, (uint32_t)(a_loads - 1) & 1, args.err, kErrWaitProducer, abort_flag)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(a_full, 4 * 16384);
+        for (int kb = 0; kb < 4; ++kb) tma_load_2d(smem + S::kA + kb * 16384, &map_a, a_full, kb * 64, m0);
+        ++a_loads;
+        auto load_g1 = [&](int c) {  // 2 stages of 2 k-blocks: W1[c*128.., k] (16 KB each)
+          for (int s = 0; s < 2 && ok; ++s) {
             uint8_t* st = next_stage(kMlpStageBytes);
             if (!st) return;
-            tma_load_2d(st, &map_a, &full[stage], kb * 64, m0);
-            tma_load_2d(st + 16384, &map_w1, &full[stage], kb * 64, c * 128);
+            tma_load_2d(st, &map_w1, &full[stage], (2 * s) * 64, c * 128);
+            tma_load_2d(st + 16384, &map_w1, &full[stage], (2 * s + 1) * 64, c * 128);
             advance();
           }
         };
@@ -156,14 +166,17 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
         load_g1(0);
         if (nch > 1) load_g1(1);
         for (int c = 0; c < nch && ok; ++c) {
-          if (c + 2 < nch) load_g1(c + 2);
           load_g2(c);
+          if (c + 2 < nch) load_g1(c + 2);
         }
       }
       if (!ok) {  // drain the copies still in flight before the CTA's shared memory is released
         const uint64_t t0 = global_ns();
         for (int j = max(0, issued - kMlpStages); j < issued; ++j)
           while (!mbar_try_wait(&full[j % kMlpStages], (j / kMlpStages) & 1) && global_ns() - t0 < kWaitLimitNs) {
+          }
+        if (a_loads > 0)
+          while (!mbar_try_wait(a_full, (uint32_t)(a_loads - 1) & 1) && global_ns() - t0 < kWaitLimitNs) {
           }
       }
     }
@@ -172,7 +185,7 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
     if (lane == 0) {
       const uint32_t idesc1 = idesc_f16(128, 128, OperandType<TIn>::kFormat, 0, 0);
       const uint32_t idesc2 = idesc_f16(128, 256, OperandType<TIn>::kFormat, 0, 0);
-      const uint32_t hbase = smem_u32(smem + S::kH);
+      const uint32_t abase = smem_u32(smem + S::kA);
       int stage = 0;
       uint32_t phase = 0;
       uint32_t gch = 0;  // chunks of all blocks before this block (acc1 / H buffer = chunk parity)
@@ -194,45 +207,49 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
           phase ^= 1;
         }
       };
+      // G1(c) into acc1[chunk parity]; the buffer's previous reader (G2 of the chunk two before) was
+      // issued earlier by this thread, and the tensor core runs MMAs in issue order
       auto g1 = [&](int c) {
-        const uint32_t gc = gch + c, b = gc & 1;
-        // the buffer held chunk gc - 2: its GELU warps must have loaded it
-        if (gc >= 2 && !wait(&a1_empty[b], ((gc - 2) >> 1) & 1)) return;
-        tc_fence_after();
-        for (int kb = 0; kb < 4 && ok; ++kb) {
+        const uint32_t b = (gch + c) & 1;
+        for (int s = 0; s < 2 && ok; ++s) {
           const uint32_t st = take_stage();
           if (!ok) return;
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            mma_f16_ss(tmem_base + b * 128, sdesc_sw128(st + kk * 32, 16, 1024),
-                       sdesc_sw128(st + 16384 + kk * 32, 16, 1024), idesc1, (kb | kk) != 0 ? 1u : 0u);
+          for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              mma_f16_ss(tmem_base + b * 128, sdesc_sw128(abase + (2 * s + kb) * 16384 + kk * 32, 16, 1024),
+                         sdesc_sw128(st + kb * 16384 + kk * 32, 16, 1024), idesc1, (s | kb | kk) != 0 ? 1u : 0u);
           release_stage();
         }
         mma_commit(&a1_full[b]);
+        if (c == nch - 1) mma_commit(a_empty);
       };
+      // G2(c): A = H in TMEM (k 0..63 at columns +0..31, k 64..127 at +64..95 of acc1[chunk parity])
       auto g2 = [&](int c) {
         const uint32_t b = (gch + c) & 1;
-        for (int kb = 0; kb < 2 && ok; ++kb) {
+        for (int s = 0; s < 2 && ok; ++s) {
           const uint32_t st = take_stage();
           if (!ok) return;
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            mma_f16_ss(tmem_base + kMlpAcc2, sdesc_sw128(hbase + b * 32768 + kb * 16384 + kk * 32, 16, 1024),
-                       sdesc_sw128(st + kk * 32, 16, 1024), idesc2, (c | kb | kk) != 0 ? 1u : 0u);
+            mma_f16_ts(tmem_base + kMlpAcc2, tmem_base + b * 128 + s * 64 + kk * 8, sdesc_sw128(st + kk * 32, 16, 1024),
+                       idesc2, (c | s | kk) != 0 ? 1u : 0u);
           release_stage();
         }
-        mma_commit(&h_empty[b]);
       };
       for (int blk = blockIdx.x; blk < args.num_blocks && ok; blk += gridDim.x, ++lb) {
+        if (!wait(a_full, (uint32_t)lb & 1)) break;
+        tc_fence_after();
         g1(0);
         if (nch > 1) g1(1);
         for (int c = 0; c < nch && ok; ++c) {
           const uint32_t gc = gch + c;
-          if (c + 2 < nch) g1(c + 2);
           if (!wait(&h_full[gc & 1], (gc >> 1) & 1)) break;
           if (c == 0 && lb > 0 && !wait(a2_empty, (uint32_t)(lb - 1) & 1)) break;
           tc_fence_after();
           g2(c);
+          if (c + 2 < nch) g1(c + 2);
         }
         if (!ok) break;
         mma_commit(a2_full);
@@ -247,8 +264,7 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
     // ------------------------------------------------------------------ GELU warps
     const int gw = warp - 2;
     const int quarter = warp & 3;
-    const int half = gw >> 2;  // columns [64 half, 64 half + 64) of the chunk = k-block `half` of H
-    const int r = quarter * 32 + lane;
+    const int half = gw >> 2;  // columns [64 half, 64 half + 64) of the chunk
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     uint32_t gc = 0;
     bool ok = true;
@@ -264,14 +280,6 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
         const uint32_t ta = tmem_base + lane_off + b * 128 + half * 64;
         tmem_ld32(ta, v0);
         tmem_ld32(ta + 32, v1);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&a1_empty[b]);  // the next G1 into this buffer may start
-        // the H buffer is free once G2 of the chunk two before has read it
-        if (gc >= 2 && !mbar_wait_warp(&h_empty[b], ((gc >> 1) & 1) ^ 1, args.err, kErrWaitEpilogue, abort_flag)) {
-          ok = false;
-          break;
-        }
         const float4* bp = reinterpret_cast<const float4*>(args.b1 + c * 128 + half * 64);
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
@@ -286,8 +294,16 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
           v0[i] = g0.x; v0[i + 1] = g0.y;
           v1[i] = g1.x; v1[i + 1] = g1.y;
         }
-        stage_slab_row<TIn>(smem + S::kH + b * 32768 + half * 16384, r, v0, v1);
-        fence_async_smem();  // generic-proxy writes -> visible to the tensor core
+        // H over this warp's own (already loaded) columns: 64 16-bit values in 32 columns
+        uint32_t p0[16], p1[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          p0[i] = OperandType<TIn>::pack2(v0[2 * i], v0[2 * i + 1]);
+          p1[i] = OperandType<TIn>::pack2(v1[2 * i], v1[2 * i + 1]);
+        }
+        tmem_st16(ta, p0);
+        tmem_st16(ta + 16, p1);
+        tmem_wait_st();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&h_full[b]);
