@@ -34,7 +34,13 @@
 namespace trc {
 
 constexpr int kAttnThreads = 352;
-constexpr int kAttnKvStages = 3;
+// Key/value stages. Frequency mode loads one stage per tile and item (tile A, tile B, tile A, ...): with an
+// even stage count, stage (2 item + tile) % kAttnKvStages is only ever used by that one tile, so each
+// tile's MMA issuer waits on every phase of its stages in order. With an odd count the tiles would share
+// stages, and a tile running an item ahead could wait on a stage whose previous phase (the other tile's
+// load) had not completed yet, where a parity wait cannot tell the two phases apart.
+constexpr int kAttnKvStages = 4;
+static_assert(kAttnKvStages % 2 == 0, "frequency mode needs per-tile stages");
 
 struct AttnArgs {
   int num_items;  // work items
@@ -55,6 +61,7 @@ struct AttnSmem {
   static constexpr int kKV = kQ + 4 * kTile;   // [stages][K, V]
   static constexpr int kBar = kKV + 2 * kAttnKvStages * kTile;
   static constexpr int kBytes = kBar + 512 + 1024;
+  static_assert(kBytes <= 232448, "shared memory per CTA");
 };
 
 // TMEM columns (all 512): S_A [0,128), S_B [128,256), P_A [256,320), P_B [320,384) (16-bit pairs),
@@ -64,7 +71,9 @@ __device__ __forceinline__ uint32_t tmem_col_p(int x) { return 256u + (uint32_t)
 __device__ __forceinline__ uint32_t tmem_col_o(int x) { return 384u + (uint32_t)x * 64u; }
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: P stays <= 2^8
 
-template <typename TIn>
+// kFreq: frequency mode (compiled separately, so each mode gets its own register allocation); it must
+// equal args.mode == 1.
+template <typename TIn, bool kFreq>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     attention_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                      const __grid_constant__ CUtensorMap map_v, const __grid_constant__ AttnArgs args) {
@@ -87,7 +96,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const bool freq = args.mode == 1;
+  constexpr bool freq = kFreq;
   const int nsteps = freq ? 1 : args.n_kv;       // key tiles per query tile and item
   const int kv_per_item = freq ? 2 : args.n_kv;  // key/value loads per item
 
@@ -266,7 +275,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         seq = bh;
         pos = (item - bh * args.q_pairs) * 256 + x * 128 + r;
       }
-      const int my_block = r >> 6;
+      // the row's output token; its gate is loaded now, so the load is long done by the epilogue
+      const bool valid = pos < args.L && seq < args.BH;
+      auto token_of = [&]() -> long {
+        const int grp = seq >> 3;
+        if (!freq) {  // grp = b*F + f, pos = t
+          const int b = grp / args.F, f = grp - b * args.F;
+          return ((long)b * args.T + pos) * args.F + f;
+        }
+        return (long)grp * args.F + pos;  // grp = b*T + t, pos = f
+      };
+      const float gate = valid ? args.G[token_of() * 8 + (seq & 7)] : 0.f;
       float m_run = -INFINITY, l_run = 0.f;
       bool ok = true;
       for (int j = 0; j < nsteps; ++j, ++g) {
@@ -275,20 +294,72 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           break;
         }
         tc_fence_after();
+        if constexpr (freq) {
+          // a row's keys are the 64 columns of its own sequence (block quarter / 2 of the tile); the other
+          // block's P is zero, and only keys < L exist. One key tile per item: no rescaling.
+          const int blk = quarter >> 1;
+          float sf[64];
+          tmem_ld64(tS + blk * 64, sf);
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&s_free[x]);
+#pragma unroll
+          for (int i = 0; i < 64; ++i)
+            if (i >= args.L) sf[i] = -INFINITY;
+          float mx4[4] = {sf[0], sf[1], sf[2], sf[3]};
+#pragma unroll
+          for (int i = 4; i < 60; i += 8) {
+            mx4[0] = fmax3(mx4[0], sf[i], sf[i + 4]);
+            mx4[1] = fmax3(mx4[1], sf[i + 1], sf[i + 5]);
+            mx4[2] = fmax3(mx4[2], sf[i + 2], sf[i + 6]);
+            mx4[3] = fmax3(mx4[3], sf[i + 3], sf[i + 7]);
+          }
+          m_run = fmaxf(fmax3(mx4[0], mx4[1], sf[60]), fmax3(mx4[2], mx4[3], fmax3(sf[61], sf[62], sf[63]))) * kLog2e;
+          const float2 scale2 = make_float2(kLog2e, kLog2e);
+          const float2 shift2 = make_float2(-m_run, -m_run);
+          float2 l2 = make_float2(0.f, 0.f);
+          uint32_t pk0[16], pk1[16];
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            const float2 xv = __ffma2_rn(make_float2(sf[i], sf[i + 1]), scale2, shift2);
+            const float2 pv = make_float2(ex2_approx(xv.x), ex2_approx(xv.y));
+            l2 = __fadd2_rn(l2, pv);
+            pk0[i >> 1] = OperandType<TIn>::pack2(pv.x, pv.y);
+            const float2 xw = __ffma2_rn(make_float2(sf[32 + i], sf[33 + i]), scale2, shift2);
+            const float2 pw = make_float2(ex2_approx(xw.x), ex2_approx(xw.y));
+            l2 = __fadd2_rn(l2, pw);
+            pk1[i >> 1] = OperandType<TIn>::pack2(pw.x, pw.y);
+          }
+          l_run = l2.x + l2.y;
+          // P and O are this tile's again once the previous item's O = P V has completed
+          if (g > 0 && !mbar_wait_warp(&p_free[x], (g - 1) & 1u, args.err, kErrWaitSoftmax, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          uint32_t z[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) z[i] = 0u;
+          tmem_st16(tP + blk * 32, pk0);
+          tmem_st16(tP + blk * 32 + 16, pk1);
+          tmem_st16(tP + (1 - blk) * 32, z);
+          tmem_st16(tP + (1 - blk) * 32 + 16, z);
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&p_full[x]);
+          continue;
+        }
         // the whole score row in registers (one TMEM read); the S columns are then free for the next S
         float sc[128];
         tmem_ld128(tS, sc);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&s_free[x]);
-        // keys outside this row's sequence -> -inf
+        // keys past the sequence's end -> -inf
         const int key0 = j * 128;
-        const int kmax = freq ? 128 : min(128, args.L - key0);  // keys of this tile that exist
-        if (freq) {
-#pragma unroll
-          for (int i = 0; i < 128; ++i)
-            if ((i >> 6) != my_block || (i & 63) >= args.L) sc[i] = -INFINITY;
-        } else if (kmax < 128) {
+        const int kmax = min(128, args.L - key0);  // keys of this tile that exist
+        if (kmax < 128) {
 #pragma unroll
           for (int i = 0; i < 128; ++i)
             if (i >= kmax) sc[i] = -INFINITY;
@@ -374,18 +445,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&o_free[x]);
-      const bool valid = pos < args.L && seq < args.BH;
       if (valid) {
+        const long token = token_of();
         const int h = seq & 7;
-        const int grp = seq >> 3;
-        long token;
-        if (!freq) {  // grp = b*F + f, pos = t
-          const int b = grp / args.F, f = grp - b * args.F;
-          token = ((long)b * args.T + pos) * args.F + f;
-        } else {  // grp = b*T + t, pos = f
-          token = (long)grp * args.F + pos;
-        }
-        const float scale = args.G[token * 8 + h] / l_run;
+        const float scale = gate / l_run;
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           o0[i] *= scale;

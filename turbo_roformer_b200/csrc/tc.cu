@@ -55,17 +55,24 @@ cudaError_t launch_gemm_p(int epi, const CUtensorMap& ma, const CUtensorMap& mb,
   }
 }
 
-template <typename T>
-cudaError_t launch_attention_t(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
+template <typename T, bool kFreq>
+cudaError_t launch_attention_m(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                                const AttnArgs& args, int num_sms, cudaStream_t st) {
-  auto kern = attention_kernel<T>;
-  static std::atomic<unsigned long long> done{0};  // one per <T> instantiation
+  auto kern = attention_kernel<T, kFreq>;
+  static std::atomic<unsigned long long> done{0};  // one per <T, kFreq> instantiation
   cudaError_t e = allow_smem(kern, AttnSmem::kBytes, done);
   if (e != cudaSuccess) return e;
   if (args.num_items <= 0) return cudaSuccess;
   const int grid = args.num_items < num_sms ? args.num_items : num_sms;
   kern<<<grid, kAttnThreads, AttnSmem::kBytes, st>>>(mq, mk, mv, args);
   return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t launch_attention_t(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
+                               const AttnArgs& args, int num_sms, cudaStream_t st) {
+  return args.mode == 1 ? launch_attention_m<T, true>(mq, mk, mv, args, num_sms, st)
+                        : launch_attention_m<T, false>(mq, mk, mv, args, num_sms, st);
 }
 
 }  // namespace
