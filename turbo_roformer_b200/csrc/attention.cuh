@@ -59,7 +59,8 @@ struct AttnSmem {
   static constexpr int kTile = 128 * 64 * 2;  // 16 KB: 128 rows x 64 dims
   static constexpr int kQ = 0;                 // [2 buffers][2 tiles]
   static constexpr int kKV = kQ + 4 * kTile;   // [stages][K, V]
-  static constexpr int kBar = kKV + 2 * kAttnKvStages * kTile;
+  static constexpr int kScale = kKV + 2 * kAttnKvStages * kTile;  // [2 tiles][128 rows] gate / l (fp32)
+  static constexpr int kBar = kScale + 2 * 128 * 4;
   static constexpr int kBytes = kBar + 512 + 1024;
   static_assert(kBytes <= 232448, "shared memory per CTA");
 };
@@ -265,7 +266,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const uint32_t tO = tmem_base + lane_off + tmem_col_o(x);
     const float kLog2e = 1.4426950408889634f;
     uint32_t g = 0;  // steps of this tile so far, all items (s_full / p_free phases)
-    for (int item = blockIdx.x; item < args.num_items; item += gridDim.x) {
+    // This thread's query row of an item: output token, false if the row lies outside its sequence.
+    auto row_token = [&](int item, long* token) -> bool {
       int seq, pos;
       if (freq) {
         seq = 4 * item + 2 * x + (r >> 6);
@@ -275,17 +277,47 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         seq = bh;
         pos = (item - bh * args.q_pairs) * 256 + x * 128 + r;
       }
-      // the row's output token; its gate is loaded now, so the load is long done by the epilogue
-      const bool valid = pos < args.L && seq < args.BH;
-      auto token_of = [&]() -> long {
-        const int grp = seq >> 3;
-        if (!freq) {  // grp = b*F + f, pos = t
-          const int b = grp / args.F, f = grp - b * args.F;
-          return ((long)b * args.T + pos) * args.F + f;
+      if (pos >= args.L || seq >= args.BH) return false;
+      const int grp = seq >> 3;
+      if (!freq) {  // grp = b*F + f, pos = t
+        const int b = grp / args.F, f = grp - b * args.F;
+        *token = (((long)b * args.T + pos) * args.F + f) * 8 + (seq & 7);
+      } else {  // grp = b*T + t, pos = f
+        *token = ((long)grp * args.F + pos) * 8 + (seq & 7);
+      }
+      return true;
+    };
+    // The epilogue of an item (read O, release it, scale by gate / l, store) is deferred until the next
+    // item's first P has been written: the wait for the item's last O += P V then overlaps that step's
+    // exponentials, and the next O = P V (which waits for o_free) starts as soon as O has been read. The
+    // row's gate / l waits in shared memory; its token is recomputed from the item index.
+    float* row_scale = reinterpret_cast<float*>(smem + S::kScale) + x * 128 + r;
+    auto finish = [&](int prev_item) {  // 32 columns at a time (register budget of the softmax warps)
+      long th;                          // token * 8 + head
+      const bool valid = row_token(prev_item, &th);
+      const float scale = *row_scale;
+      TIn* dst = static_cast<TIn*>(args.O) + th * 64;  // [token][h*64 + d]
+#pragma unroll 1
+      for (int hc = 0; hc < 2; ++hc) {
+        float o[32];
+        tmem_ld32(tO + hc * 32, o);
+        if (hc == 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&o_free[x]);
         }
-        return (long)grp * args.F + pos;  // grp = b*T + t, pos = f
-      };
-      const float gate = valid ? args.G[token_of() * 8 + (seq & 7)] : 0.f;
+        if (valid) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] *= scale;
+          store32<TIn>(dst + hc * 32, o);
+        }
+      }
+    };
+    bool alive = true;
+    for (int item = blockIdx.x; item < args.num_items && alive; item += gridDim.x) {
+      // the row's gate, loaded now so the load is long done when the item ends
+      long th0;
+      const float gate = row_token(item, &th0) ? args.G[th0] : 0.f;
       float m_run = -INFINITY, l_run = 0.f;
       bool ok = true;
       for (int j = 0; j < nsteps; ++j, ++g) {
@@ -348,6 +380,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&p_full[x]);
+          if (item != (int)blockIdx.x) finish(item - gridDim.x);  // its O = P V completed: p_free above
           continue;
         }
         // the whole score row in registers (one TMEM read); the S columns are then free for the next S
@@ -434,30 +467,20 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[x]);
+        // step 0 waited (p_free) for the previous item's last O += P V and did not rescale O
+        if (j == 0 && item != (int)blockIdx.x) finish(item - gridDim.x);
       }
-      if (!ok) break;
-      // epilogue: O is final once the last O += P V completed; out = O / l * gate -> O[token][h*64 + d]
-      if (!mbar_wait_warp(&p_free[x], (g - 1) & 1u, args.err, kErrWaitSoftmax, abort_flag)) break;
+      if (!ok) {
+        alive = false;
+        break;
+      }
+      *row_scale = gate / l_run;  // read back by this thread's deferred epilogue
+    }
+    // the last item: O is final once its last O += P V completed
+    if (alive && (int)blockIdx.x < args.num_items &&
+        mbar_wait_warp(&p_free[x], (g - 1) & 1u, args.err, kErrWaitSoftmax, abort_flag)) {
       tc_fence_after();
-      float o0[32], o1[32];
-      tmem_ld32(tO, o0);
-      tmem_ld32(tO + 32, o1);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&o_free[x]);
-      if (valid) {
-        const long token = token_of();
-        const int h = seq & 7;
-        const float scale = gate / l_run;
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          o0[i] *= scale;
-          o1[i] *= scale;
-        }
-        TIn* dst = static_cast<TIn*>(args.O) + token * 512 + h * 64;
-        store32<TIn>(dst, o0);
-        store32<TIn>(dst + 32, o1);
-      }
+      finish(blockIdx.x + ((args.num_items - 1 - (int)blockIdx.x) / (int)gridDim.x) * gridDim.x);
     }
   }
 
