@@ -44,11 +44,11 @@ PUBLISHED = 1.38  # reference, 252.39 s song / 183.0 s wall on 8 Zen 4 cores (do
 # `ncu --set full` on `bench.py --batch 1` (the one-chunk captures summarised under profiles/); a batched
 # launch moves this per chunk. None = not captured.
 TRAFFIC_PER_CHUNK = {
-    "attention_t": (327.66e6 + 88.15e6),
-    "attention_f": (327.25e6 + 83.65e6),
+    "attention_t": (328.18e6 + 87.41e6),
+    "attention_f": (327.21e6 + 77.37e6),
     "qkv_rope_gemm": (56.79e6 + 269.93e6),
     "gemm_out_res_norm": (216.26e6 + 104.90e6),
-    "ffn_res_norm": (163.13e6 + 103.20e6),
+    "ffn_res_norm": (163.27e6 + 102.98e6),
 }
 
 
