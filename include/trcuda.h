@@ -101,8 +101,8 @@ int trc_ola(const float* d_chunks, int64_t chunk_out_len, const int64_t* h_start
 const char* trc_last_error(void);
 
 /* Overlap-add that allocates nothing. No counterpart in the reference: it exists for callers that may
- * not allocate device memory while they run (a host application capturing its processing into a CUDA
- * graph, a plugin whose host owns all device memory, a real-time audio thread that must not enter the
+ * not allocate device memory while they run (an audio plugin whose host application owns all device
+ * memory and forbids allocations of its own, a real-time audio thread that must not block in the
  * allocator). Same arguments, semantics and result as trc_ola, but the Hamming window and the chunk
  * starts are staged in fixed arrays inside this library (one set per GPU that loads it, kept until the
  * process exits: TRC_OLA_NOALLOC_MAX_CHUNK floats + TRC_OLA_NOALLOC_MAX_CHUNKS int64, about 8 MiB).

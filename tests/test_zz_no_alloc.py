@@ -1,6 +1,6 @@
-"""trc_ola_noalloc, the overlap-add for callers that cannot allocate device memory while they run (a host
-application capturing its audio processing into a CUDA graph, a plugin whose host owns the device memory,
-a real-time audio thread). Its output must equal the allocating trc_ola exactly (the overlap-add is
+"""trc_ola_noalloc, the overlap-add for callers that cannot allocate device memory while they run (an
+audio plugin whose host application owns the device memory, a real-time audio thread that must not block
+in the allocator). Its output must equal the allocating trc_ola exactly (the overlap-add is
 bit-identical to the reference), on two calls in a row, because every call reuses the same fixed
 staging arrays inside the library. This file is named to be collected last."""
 

@@ -1,12 +1,13 @@
 // trc_ola_noalloc: the chunk overlap-add for callers that cannot allocate device memory.
 //
 // trc_ola stages the Hamming window and the chunk starts in buffers it obtains with cudaMallocAsync.
-// Some callers cannot allow that: code running inside a captured CUDA graph region of a host
-// application, plugins whose host application owns all device memory through its own pool and forbids
-// driver allocations, or real-time audio hosts that must not take the allocator's locks on their
-// processing thread. For them this entry point keeps the two staging arrays in fixed, file-scope
-// device arrays of this library instead. They exist once per GPU that loads the library and stay
-// allocated until the process exits (8 MiB + 64 KiB per GPU).
+// Some callers cannot allow that: audio plugins whose host application owns all device memory through
+// its own pool and forbids allocations of their own, or real-time audio hosts that must not take the
+// allocator's locks on their processing thread. For them this entry point keeps the two staging arrays
+// in fixed, file-scope device arrays of this library instead. They exist once per GPU that loads the
+// library and stay allocated until the process exits (8 MiB + 64 KiB per GPU). The first call on a
+// device looks up the arrays' device addresses (a one-time set-up, which should come before any stream
+// capture); every call shares the arrays, so calls that may overlap on the GPU race.
 #include <cuda_runtime.h>
 
 #include <cmath>
