@@ -77,6 +77,24 @@ def test_full_chunk_matches_fp32_reference(full_cfg, full_sd, golden_full, cuda_
     assert snr_db(ref, y) >= 50.0
 
 
+@pytest.mark.slow
+def test_full_model_batch4_equals_single_chunks(full_cfg, full_sd, cuda_device):
+    """The bench's shape (four Separator chunks per forward through the full model) is clean and
+    bit-identical to one chunk per forward, repeated: the persistent kernels walk ~90 work items per CTA
+    here, where a pipeline that lets one query tile run an item ahead would surface."""
+    from turbo_roformer_b200.backend import CudaBSRoformer
+
+    m = CudaBSRoformer(full_sd, cfg=full_cfg, device=0, precision="fp16")
+    C = 749_259
+    song = torch.from_numpy(S.song_audio(4 * C / 44100 + 0.1, seed=3)).cuda()
+    frames = torch.stack([song[:, k * C : (k + 1) * C] for k in range(4)]).contiguous()
+    singles = torch.cat([m.forward_device(frames[k : k + 1]) for k in range(4)])
+    for _ in range(3):
+        y = m.forward_device(frames)  # checks the device error word
+        assert torch.isfinite(y).all()
+        assert torch.equal(y, singles)
+
+
 def test_bounded_wait_reports_and_recovers(tiny_cuda, tiny_cfg):
     """A pipeline wait that can never complete ends with TRC_E_DEVICE after the wait limit, not a hang or
     a fault, and the handle keeps working (the failure path of every pipelined kernel)."""
