@@ -189,7 +189,7 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
-    ap.add_argument("--batch", type=int, default=4, help="chunks per forward call")
+    ap.add_argument("--batch", type=int, default=8, help="chunks per forward call (8: 8+8+8+5 for the song)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.impl == "reference":
