@@ -28,6 +28,32 @@ def test_invalid_input_raises(bad):
         audio.as_channels_first(bad)
 
 
+def _fold_by_rule(x):
+    """The separator's surround fold written out channel by channel (turbo_roformer/audio.py:35-59):
+    centre to both sides at -3 dB, LFE of >= 6 channels dropped, the rest alternately left/right at
+    -3 dB, each side divided by its summed gains."""
+    g = 0.7071
+    sides = [[(0, 1.0)], [(1, 1.0)]]
+    if x.shape[0] >= 3:
+        sides[0].append((2, g))
+        sides[1].append((2, g))
+    for k, ch in enumerate(range(4 if x.shape[0] >= 6 else 3, x.shape[0])):
+        sides[k % 2].append((ch, g))
+    out = [sum(w * x[ch].astype(np.float64) for ch, w in s) / sum(w for _, w in s) for s in sides]
+    return np.stack(out).astype(np.float32)
+
+
+@pytest.mark.parametrize("channels", [3, 4, 5, 6, 7, 8, 16])
+def test_surround_fold_matches_the_channel_rule(channels):
+    rng = np.random.default_rng(channels)
+    x = rng.standard_normal((channels, 1000)).astype(np.float32)
+    np.testing.assert_allclose(audio.to_stereo(x), _fold_by_rule(x), rtol=1e-6, atol=1e-7)
+    if channels >= 6:  # the LFE never reaches the output
+        lfe_only = np.zeros_like(x)
+        lfe_only[3] = x[3]
+        assert not audio.to_stereo(lfe_only).any()
+
+
 def test_downmix_keeps_centre():
     rng = np.random.default_rng(2)
     six = rng.standard_normal((6, 1000)).astype(np.float32)
@@ -39,6 +65,16 @@ def test_downmix_keeps_centre():
     assert audio.to_stereo(six).shape == (2, 1000)
     mono = six[:1]
     np.testing.assert_array_equal(audio.to_stereo(mono), np.repeat(mono, 2, axis=0))
+    stereo = six[:2]
+    np.testing.assert_array_equal(audio.to_stereo(stereo), stereo)
+
+
+def test_resample_length_rule_without_rate_change():
+    x = np.arange(20, dtype=np.float32).reshape(2, 10)
+    np.testing.assert_array_equal(audio.resample(x, 44100, 44100, length=7), x[:, :7])
+    padded = audio.resample(x, 44100, 44100, length=12)
+    np.testing.assert_array_equal(padded[:, :10], x)
+    assert not padded[:, 10:].any()
 
 
 def _bare(chunk=16256, hop=128):

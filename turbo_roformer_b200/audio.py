@@ -1,17 +1,27 @@
-"""Host-side audio helpers of the Separator contract (turbo_roformer/audio.py:16-131).
+"""What ``Separator`` does to a mix before the model and to the result after it, on the host.
 
-Validation, channel layout and downmix are restated here because ``Separator.separate`` applies them
-before the model; resampling (soxr) and file I/O (soundfile) are optional dependencies, imported on use
-exactly like the reference does.
+The separator contract (turbo_roformer/separator.py:203-283, its input rules in turbo_roformer/audio.py):
+float input of shape (channels, samples) or (samples,); integer PCM, NaN/inf, empty arrays and arrays
+that look transposed are refused with ``ValueError``; mono is played on both sides, more than two
+channels are folded to stereo, and rates other than 44.1 kHz are resampled around the model.
+
+Channel handling here is one linear map: a (2, C) gain matrix per channel count, applied in float64.
+The fold of a surround layout sends the centre (channel 2) to both sides at -3 dB, drops the LFE
+(channel 3) of 5.1 and wider layouts, spreads the remaining channels alternately left and right at
+-3 dB, and scales each output side by the inverse of its total gain. Resampling (``soxr``) and file
+I/O (``soundfile``) are optional dependencies that are imported only when a call needs them.
 """
 
 from __future__ import annotations
 
 import os
+from functools import lru_cache
 
 import numpy as np
 
 MAX_CHANNELS = 16
+SIDE_GAIN = 0.7071  # -3 dB
+FORMATS = {"wav": "FLOAT", "flac": "PCM_24"}  # output container -> sample encoding
 
 
 def check_finite(a: np.ndarray) -> None:
@@ -20,87 +30,94 @@ def check_finite(a: np.ndarray) -> None:
 
 
 def as_channels_first(mix, finite: bool = True) -> np.ndarray:
-    """Validate and convert to float32 (channels, samples); raises ValueError like audio.py:16-32.
+    """The mix as a float32 (channels, samples) array; ``ValueError`` for input the separator refuses.
 
-    ``finite=False`` leaves the NaN/inf scan to the caller (the CUDA separator runs it on the device)."""
+    ``finite=False`` skips the NaN/inf scan (the CUDA separator makes it on the device instead)."""
     a = np.asarray(mix)
     if a.dtype.kind != "f":
-        raise ValueError(f"expected a floating point array (got dtype {a.dtype}); scale integer PCM to [-1, 1] first")
-    if a.ndim == 1:
-        a = a[None, :]
-    elif a.ndim != 2:
+        raise ValueError(f"expected floating point samples, got dtype {a.dtype} (scale integer PCM to [-1, 1])")
+    if a.ndim not in (1, 2):
         raise ValueError(f"expected (channels, samples) or (samples,), got shape {a.shape}")
-    if a.shape[0] > MAX_CHANNELS:
-        raise ValueError(f"got {a.shape[0]} channels - is the array (samples, channels)? pass mix.T")
-    if a.shape[0] == 0 or a.shape[1] == 0:
+    a = a.reshape(1, -1) if a.ndim == 1 else a
+    channels, samples = a.shape
+    if channels > MAX_CHANNELS:
+        raise ValueError(f"{channels} channels: the array looks like (samples, channels); pass mix.T")
+    if channels * samples == 0:
         raise ValueError("empty input")
-    a = a.astype(np.float32, copy=False)
+    a = np.asarray(a, dtype=np.float32)
     if finite:
         check_finite(a)
     return a
 
 
-def downmix_stereo(x: np.ndarray) -> np.ndarray:
-    """(C > 2, n) -> (2, n): centre into both sides at -3 dB, LFE dropped for C >= 6, other channels
-    alternately left/right at -3 dB, each side normalised by its summed gains (audio.py:35-59)."""
-    c = x.shape[0]
-    g = 0.7071
-    left = x[0].astype(np.float64)
-    right = x[1].astype(np.float64)
-    gl = gr = 1.0
-    if c >= 3:
-        left = left + g * x[2]
-        right = right + g * x[2]
-        gl += g
-        gr += g
-    extra = range(4 if c >= 6 else 3, c)
-    for k, ch in enumerate(extra):
-        if k % 2 == 0:
-            left = left + g * x[ch]
-            gl += g
-        else:
-            right = right + g * x[ch]
-            gr += g
-    return np.stack([left / gl, right / gr]).astype(np.float32)
+@lru_cache(maxsize=MAX_CHANNELS)
+def stereo_gains(channels: int) -> np.ndarray:
+    """(2, channels) float64 matrix that maps a layout of ``channels`` channels to (left, right)."""
+    if channels < 1:
+        raise ValueError("need at least one channel")
+    if channels == 1:
+        return np.ones((2, 1))
+    m = np.zeros((2, channels))
+    m[0, 0] = m[1, 1] = 1.0
+    if channels >= 3:
+        m[:, 2] = SIDE_GAIN
+    first_extra = 4 if channels >= 6 else 3  # skip the LFE of 5.1 and wider
+    for k, ch in enumerate(range(first_extra, channels)):
+        m[k % 2, ch] = SIDE_GAIN
+    m /= m.sum(axis=1, keepdims=True)
+    m.setflags(write=False)
+    return m
 
 
 def to_stereo(x: np.ndarray) -> np.ndarray:
-    """Mono duplicated, stereo passed through, more channels downmixed (audio.py:62-68)."""
-    if x.shape[0] == 1:
-        return np.repeat(x, 2, axis=0)
+    """(C, n) float32 -> (2, n) float32 through ``stereo_gains(C)``; stereo input is passed through."""
     if x.shape[0] == 2:
-        return np.ascontiguousarray(x)
-    return downmix_stereo(x)
+        return np.ascontiguousarray(x, dtype=np.float32)
+    if x.shape[0] == 1:
+        return np.ascontiguousarray(np.broadcast_to(x, (2, x.shape[1])), dtype=np.float32)
+    return (stereo_gains(x.shape[0]) @ x.astype(np.float64)).astype(np.float32)
+
+
+def downmix_stereo(x: np.ndarray) -> np.ndarray:
+    """Fold of a layout with more than two channels (kept as a name for callers of the reference API)."""
+    if x.shape[0] <= 2:
+        raise ValueError("downmix needs more than two channels")
+    return to_stereo(x)
 
 
 def resample(x: np.ndarray, sr_in: int, sr_out: int, length: int | None = None) -> np.ndarray:
-    """(C, n) -> (C, m) with soxr HQ; ``length`` forces the output length (audio.py:71-82)."""
+    """(C, n) at ``sr_in`` -> (C, m) at ``sr_out`` (soxr, high quality); ``length`` trims or zero-pads
+    the result to exactly that many samples."""
+    y = np.asarray(x, dtype=np.float32)
     if sr_in != sr_out:
-        import soxr  # optional dependency, as in the reference
-
-        y = soxr.resample(np.ascontiguousarray(x.T), sr_in, sr_out, quality="HQ").T
-        y = np.asarray(y, dtype=np.float32).reshape(x.shape[0], -1)
-    else:
-        y = x
-    if length is not None and y.shape[1] != length:
-        y = y[:, :length] if y.shape[1] > length else np.pad(y, ((0, 0), (0, length - y.shape[1])))
+        try:
+            import soxr
+        except ImportError as e:  # pragma: no cover - depends on the environment
+            raise ImportError(f"resampling {sr_in} Hz -> {sr_out} Hz needs the optional package 'soxr'") from e
+        y = np.asarray(soxr.resample(np.ascontiguousarray(y.T), sr_in, sr_out, quality="HQ"), dtype=np.float32)
+        y = y.reshape(-1, x.shape[0]).T
+    if length is not None:
+        m = y.shape[1]
+        y = y[:, :length] if m >= length else np.concatenate([y, np.zeros((y.shape[0], length - m), np.float32)], 1)
     return np.ascontiguousarray(y, dtype=np.float32)
 
 
-def load(path: str | os.PathLike) -> tuple[np.ndarray, int]:
-    """Read an audio file -> ((channels, samples) float32, sample rate) via soundfile (optional dependency)."""
-    import soundfile as sf
-
-    data, sr = sf.read(str(path), dtype="float32", always_2d=True)
-    return np.ascontiguousarray(data.T), int(sr)
-
-
 def output_formats() -> tuple[str, ...]:
-    return ("wav", "flac")
+    return tuple(FORMATS)
+
+
+def load(path: str | os.PathLike) -> tuple[np.ndarray, int]:
+    """Decode an audio file into (float32 (channels, samples), sample rate); needs 'soundfile'."""
+    import soundfile
+
+    frames, sr = soundfile.read(os.fspath(path), dtype="float32", always_2d=True)
+    return np.ascontiguousarray(frames.T), int(sr)
 
 
 def write(path: str | os.PathLike, data: np.ndarray, sr: int, fmt: str = "wav") -> None:
-    import soundfile as sf
+    """Encode (channels, samples) float32 as ``fmt`` (float WAV or 24-bit FLAC); needs 'soundfile'."""
+    import soundfile
 
-    subtype = "FLOAT" if fmt == "wav" else "PCM_24"
-    sf.write(str(path), np.ascontiguousarray(data.T), sr, subtype=subtype, format=fmt.upper())
+    if fmt not in FORMATS:
+        raise ValueError(f"unsupported output format {fmt!r}")
+    soundfile.write(os.fspath(path), np.ascontiguousarray(data.T), sr, subtype=FORMATS[fmt], format=fmt.upper())
