@@ -75,6 +75,11 @@ void trc_destroy(trc_handle* h);
 int trc_forward(trc_handle* h, const float* d_audio, int batch, int64_t samples, float* d_out, void* stream);
 int64_t trc_output_length(const trc_handle* h, int64_t samples);
 
+/* Replaces FastBSRoformer._transformer_cpp (turbo_roformer/fast.py:269-341): the 2*depth time/frequency
+ * transformers alone on the fp32 residual stream d_X [batch * T * n_bands][256] (token order
+ * (batch, frame, band)), updated in place. Uses the handle's work buffers; asynchronous on `stream`. */
+int trc_transformer(trc_handle* h, float* d_X, int batch, int T, void* stream);
+
 /* Synchronises `stream` and returns TRC_E_DEVICE if a kernel of this handle recorded a device error
  * since the last check (the error word is then cleared). */
 int trc_check(trc_handle* h, void* stream);
@@ -104,12 +109,14 @@ const char* trc_last_error(void);
  * not allocate device memory while they run (an audio plugin whose host application owns all device
  * memory and forbids allocations of its own, a real-time audio thread that must not block in the
  * allocator). Same arguments, semantics and result as trc_ola, but the Hamming window and the chunk
- * starts are staged in fixed arrays inside this library (one set per GPU that loads it, kept until the
- * process exits: TRC_OLA_NOALLOC_MAX_CHUNK floats + TRC_OLA_NOALLOC_MAX_CHUNKS int64, about 8 MiB).
- * Longer chunks or more chunks are rejected with TRC_E_INVALID. The first call on a device looks the
- * arrays up (one-time set-up); make that first call before any stream capture. All calls share the
- * arrays: calls that may overlap on the GPU (different streams, or different host threads on one
- * device) race and must be serialised by the caller. */
+ * starts are staged in fixed arrays inside this library (one set per GPU context that loads it, kept
+ * until the process exits: TRC_OLA_NOALLOC_MAX_CHUNK floats + TRC_OLA_NOALLOC_MAX_CHUNKS int64, about
+ * 8 MiB). Longer chunks or more chunks are rejected with TRC_E_INVALID. The first call in a CUDA context
+ * looks the arrays up (one-time set-up); make that first call before any stream capture. The window is
+ * uploaded (from pageable host memory) only when the chunk length differs from the last one uploaded in
+ * that context; every call uploads its starts, 8 bytes per chunk, from pageable host memory. All calls
+ * share the arrays: calls that may overlap on the GPU (different streams, or different host threads on
+ * one device) race and must be serialised by the caller. */
 #define TRC_OLA_NOALLOC_MAX_CHUNK (1 << 21)
 #define TRC_OLA_NOALLOC_MAX_CHUNKS 8192
 int trc_ola_noalloc(const float* d_chunks, int64_t chunk_out_len, const int64_t* h_starts, int n_chunks,

@@ -15,7 +15,7 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 from oracle import chunking_oracle as O
-from turbo_roformer_b200.distributed import ola_torch, separate_sharded, shard_bounds
+from turbo_roformer_b200.distributed import ola_torch, separate_from_host, separate_sharded, shard_bounds, shard_span
 
 
 def _free_port() -> int:
@@ -47,6 +47,21 @@ def _worker(rank, world, port, n, chunk, overlap, mode, q):
             for i, s in enumerate(starts):
                 out[i] = fake_model(x[:, s : s + C].unsqueeze(0))[0]
 
+        if mode == "host":  # the song stays in host memory; each rank reads its span, the peak is reduced
+            x = 3.0 * x
+
+            def run_span(span, starts, out):
+                for i, s in enumerate(starts):
+                    out[i] = fake_model(span[:, s : s + C].unsqueeze(0))[0]
+
+            res = separate_from_host(x, chunk, overlap, run_span, out_len, torch.device("cpu"), ola_torch)
+            if rank == 0:
+                ref = torch.from_numpy(O.separate_44k(x.numpy(), chunk, 64, overlap, fake_model))
+                q.put(("ok", bool(torch.equal(res, ref)), float((res - ref).abs().max())))
+            else:
+                q.put(("ok", res is None, 0.0))
+            dist.destroy_process_group()
+            return
         res = separate_sharded(run_shard, n, chunk, overlap, out_len, torch.device("cpu"), ola_torch)
         if rank == 0:
             ref = O.overlap_add(x, chunk, overlap, fake_model)
@@ -91,6 +106,25 @@ def test_two_rank_gather_equals_single_process(n, chunk, overlap):
     for r in res:
         assert r[0] == "ok", r
         assert r[1], r
+
+
+@pytest.mark.parametrize("world,n,chunk,overlap", [(2, 20_000, 3000, 2.0), (3, 9_001, 3000, 3.0)])
+def test_host_resident_song_with_reduced_peak_equals_single_process(world, n, chunk, overlap):
+    """Spans copied per rank, the peak gain from a max over ranks: equal to the one-process separator."""
+    res = _run(world, n, chunk, overlap, mode="host")
+    assert len(res) == world, res
+    for r in res:
+        assert r[0] == "ok", r
+        assert r[1], r
+
+
+def test_shard_spans_cover_the_song():
+    starts = list(range(0, 26_000, 1500)) + [27_000]
+    for world in (1, 2, 3, 8):
+        spans = [shard_span(starts, 3000, lo, hi) for lo, hi in shard_bounds(len(starts), world)]
+        cover = sorted(s for s in spans if s[1] > s[0])
+        assert cover[0][0] == 0 and cover[-1][1] == 30_000
+        assert all(a[1] >= b[0] for a, b in zip(cover, cover[1:]))
 
 
 def test_failing_rank_is_detected_by_survivor():

@@ -62,19 +62,42 @@ def test_rejects_bad_shapes(tiny_cuda):
         tiny_cuda(torch.zeros(1, 2, 100))  # not more than n_fft / 2 samples
 
 
-@pytest.mark.slow
-def test_full_chunk_matches_fp32_reference(full_cfg, full_sd, golden_full, cuda_device):
-    """Config 1: one 17 s chunk (749,700 samples) through the full 12-layer model, >= 50 dB."""
-    from turbo_roformer_b200.backend import CudaBSRoformer
-
-    m = CudaBSRoformer(full_sd, cfg=full_cfg, device=0, precision="fp16")
+@pytest.fixture(scope="module")
+def full_chunk_ref(full_cfg, full_sd, golden_full):
+    """Config 1 input (one 749,700-sample chunk) and the fp32 oracle's output for it."""
     x = torch.from_numpy(S.chunk_audio(749_700, seed=0)).unsqueeze(0)
-    y = m(x)[0].numpy()
-    torch.set_num_threads(max(1, torch.get_num_threads()))
     ref = R.forward(x, full_sd, full_cfg)[0].numpy()
     # the oracle run here is the one pinned by the reference's own output
     assert snr_db(golden_full["excerpt"], ref[:, 300_000:304_096]) >= 100.0
-    assert snr_db(ref, y) >= 50.0
+    return x, ref
+
+
+@pytest.mark.slow
+def test_full_chunk_matches_fp32_reference(full_cfg, full_sd, full_chunk_ref, cuda_device):
+    """Config 1: one 17 s chunk (749,700 samples) through the full 12-layer model, >= 50 dB."""
+    from turbo_roformer_b200.backend import CudaBSRoformer
+
+    x, ref = full_chunk_ref
+    m = CudaBSRoformer(full_sd, cfg=full_cfg, device=0, precision="fp16")
+    y = m(x)[0].numpy()
+    snr = snr_db(ref, y)
+    print(f"config 1, fp16 operands: {snr:.2f} dB vs the fp32 reference forward")
+    assert snr >= 50.0
+
+
+@pytest.mark.slow
+def test_full_chunk_bf16_operands(full_cfg, full_sd, full_chunk_ref, cuda_device):
+    """Config 1 with bf16 tensor-core operands (the north star's operand type). At these random-init
+    weights bf16 rounding alone costs the reference's own bf16 kernels their 50 dB (46.8 dB,
+    golden_meta.json); the number is recorded, and held to the reference's band minus 3 dB."""
+    from turbo_roformer_b200.backend import CudaBSRoformer
+
+    x, ref = full_chunk_ref
+    m = CudaBSRoformer(full_sd, cfg=full_cfg, device=0, precision="bf16")
+    y = m(x)[0].numpy()
+    snr = snr_db(ref, y)
+    print(f"config 1, bf16 operands: {snr:.2f} dB vs the fp32 reference forward")
+    assert snr >= 43.8
 
 
 @pytest.mark.slow

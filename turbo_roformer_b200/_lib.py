@@ -64,6 +64,7 @@ SIGNATURES = {
     "trc_destroy": (None, [c_vp]),
     "trc_forward": (c_int, [c_vp, c_vp, c_int, c_i64, c_vp, c_vp]),
     "trc_output_length": (c_i64, [c_vp, c_i64]),
+    "trc_transformer": (c_int, [c_vp, c_vp, c_int, c_int, c_vp]),
     "trc_check": (c_int, [c_vp, c_vp]),
     "trc_error_async": (c_int, [c_vp, c_vp, c_vp]),
     "trc_selftest_wait_timeout": (c_int, [c_vp, c_vp]),

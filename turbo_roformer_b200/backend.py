@@ -158,6 +158,20 @@ class CudaBSRoformer:
                 self.check()
         return out
 
+    def transformer_device(self, X: torch.Tensor, batch: int, T: int, check: bool = True) -> torch.Tensor:
+        """The 2*depth transformers alone (``FastBSRoformer._transformer_cpp``, fast.py:269-341) on the fp32
+        residual stream X (batch * T * n_bands, dim) on this GPU, updated in place and returned."""
+        if X.shape != (batch * T * self.cfg.n_bands, self.cfg.dim) or X.dtype != torch.float32:
+            raise ValueError(f"expected X of shape ({batch * T * self.cfg.n_bands}, {self.cfg.dim}) float32")
+        if X.device != self.device or not X.is_contiguous():
+            raise ValueError("X must be a contiguous tensor on the model's device")
+        with self._lock, torch.cuda.device(self.device):
+            _lib.check(self.lib.trc_transformer(self.handle, ctypes.c_void_p(X.data_ptr()), batch, T,
+                                                ctypes.c_void_p(self.stream_ptr())))
+            if check:
+                self.check()
+        return X
+
     @torch.inference_mode()
     def forward(self, raw_audio: torch.Tensor) -> torch.Tensor:
         """(B, 2, samples) float32 -> (B, 2, hop * (samples // hop)), on the input's device."""

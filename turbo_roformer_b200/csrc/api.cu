@@ -220,6 +220,14 @@ namespace {
 
 std::atomic<long long> g_launches{0};
 
+}  // namespace
+
+namespace trc {
+void count_launches(int n) { g_launches += n; }
+}  // namespace trc
+
+namespace {
+
 cudaEvent_t pool_event(trc_handle* h) {
   if (!h->ev_pool.empty()) {
     cudaEvent_t e = h->ev_pool.back();
@@ -635,6 +643,39 @@ int run_mask(trc_handle* h, const void* xn, int B, int T, float* mask, void* hid
 
 int frames_for(const trc_handle* h, int64_t samples) { return (int)(1 + samples / h->hop); }
 
+// The 2*depth transformers of fast.py:269-341 on the residual stream X [batch*T*bands][256] fp32 (updated
+// in place): the first norm, then per transformer qkv + rotary, attention, out-projection + residual +
+// norm, feed-forward + residual + norm. The last normalised stream is left in h->xn (the mask's input).
+int run_transformers(trc_handle* h, float* X, int batch, int T, cudaStream_t st) {
+  const int64_t rows = (int64_t)batch * T * h->nb;
+  int rc;
+  {
+    Section sec(h, "norm", st);
+    trc::launch_rownorm(X, h->xn.p, rows, 1e-12f, h->prec, st);
+  }
+  if ((rc = check_launch(cudaGetLastError(), "norm"))) return rc;
+  for (int l = 0; l < 2 * h->depth; ++l) {
+    const int mode = l & 1;
+    {
+      Section sec(h, "qkv_rope_gemm", st);
+      if ((rc = run_qkv(h, l, h->xn.p, batch, T, h->Q.p, h->K.p, h->V.p, h->G.p, st))) return rc;
+    }
+    {
+      Section sec(h, mode == 0 ? "attention_t" : "attention_f", st);
+      if ((rc = run_attention(h, mode, h->Q.p, h->K.p, h->V.p, h->G.p, h->O.p, batch, T, st))) return rc;
+    }
+    {
+      Section sec(h, "gemm_out_res_norm", st);
+      if ((rc = run_res_norm(h, l, 0, h->O.p, X, h->xn.p, rows, st))) return rc;
+    }
+    {
+      Section sec(h, "ffn_res_norm", st);
+      if ((rc = run_ffn(h, l, h->xn.p, X, h->xn.p, rows, st))) return rc;
+    }
+  }
+  return TRC_OK;
+}
+
 }  // namespace
 
 // ================================================================================================ C ABI
@@ -893,7 +934,6 @@ int trc_forward(trc_handle* h, const float* d_audio, int batch, int64_t samples,
   cudaStream_t st = (cudaStream_t)stream;
   int rc;
   if ((rc = ensure_workspace(h, batch, T))) return rc;
-  const int64_t rows = (int64_t)batch * T * h->nb;
   {
     Section sec(h, "stft", st);
     trc::launch_stft(d_audio, batch, samples, T, h->n_fft, h->hop, h->window.p, h->tw_fwd.p, h->xin.p, st);
@@ -902,30 +942,8 @@ int trc_forward(trc_handle* h, const float* d_audio, int batch, int64_t samples,
     Section sec(h, "band_split", st);
     trc::launch_band_split(h->xin.p, h->width, batch * T, h->nb, h->bs_off.p, h->bs_wt.p, h->bs_bias.p, h->X.p, st);
   }
-  {
-    Section sec(h, "norm", st);
-    trc::launch_rownorm(h->X.p, h->xn.p, rows, 1e-12f, h->prec, st);
-  }
   if ((rc = check_launch(cudaGetLastError(), "stft/band split"))) return rc;
-  for (int l = 0; l < 2 * h->depth; ++l) {
-    const int mode = l & 1;
-    {
-      Section sec(h, "qkv_rope_gemm", st);
-      if ((rc = run_qkv(h, l, h->xn.p, batch, T, h->Q.p, h->K.p, h->V.p, h->G.p, st))) return rc;
-    }
-    {
-      Section sec(h, mode == 0 ? "attention_t" : "attention_f", st);
-      if ((rc = run_attention(h, mode, h->Q.p, h->K.p, h->V.p, h->G.p, h->O.p, batch, T, st))) return rc;
-    }
-    {
-      Section sec(h, "gemm_out_res_norm", st);
-      if ((rc = run_res_norm(h, l, 0, h->O.p, h->X.p, h->xn.p, rows, st))) return rc;
-    }
-    {
-      Section sec(h, "ffn_res_norm", st);
-      if ((rc = run_ffn(h, l, h->xn.p, h->X.p, h->xn.p, rows, st))) return rc;
-    }
-  }
+  if ((rc = run_transformers(h, h->X.p, batch, T, st))) return rc;
   {
     Section sec(h, "mask", st, 2);
     if ((rc = run_mask(h, h->xn.p, batch, T, h->mask.p, h->H.p, st))) return rc;
@@ -936,6 +954,15 @@ int trc_forward(trc_handle* h, const float* d_audio, int batch, int64_t samples,
                       st);
   }
   return check_launch(cudaGetLastError(), "istft");
+}
+
+int trc_transformer(trc_handle* h, float* d_X, int batch, int T, void* stream) {
+  TRC_REQUIRE_PREPARED(h);
+  if (!d_X || batch < 1 || T < 1) return fail(TRC_E_INVALID, "bad transformer arguments");
+  if ((int64_t)batch * T * h->nb >= (1ll << 31) / 512) return fail(TRC_E_INVALID, "batch too large");
+  int rc;
+  if ((rc = ensure_workspace(h, batch, T))) return rc;
+  return run_transformers(h, d_X, batch, T, (cudaStream_t)stream);
 }
 
 int trc_profile(trc_handle* h, int enable) {

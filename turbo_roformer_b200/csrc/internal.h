@@ -11,6 +11,9 @@ struct GemmArgs;
 struct AttnArgs;
 struct MlpArgs;
 
+// api.cu: adds kernels launched outside api.cu to the count trc_launch_count reports
+void count_launches(int n);
+
 // dsp.cu
 void launch_stft(const float* audio, int B, int64_t L, int T, int n, int hop, const float* window, const float2* tw,
                  float* xin, cudaStream_t st);

@@ -75,6 +75,62 @@ def separate_sharded(
     return ola(allc, starts, C, n)
 
 
+def shard_span(starts: list[int], chunk: int, lo: int, hi: int) -> tuple[int, int]:
+    """Sample range [a, b) that the chunks lo..hi-1 of ``starts`` read (empty for an empty shard)."""
+    return (starts[lo], starts[hi - 1] + chunk) if hi > lo else (0, 0)
+
+
+def separate_from_host(
+    mix: torch.Tensor,
+    chunk: int,
+    overlap: float,
+    run_span: Callable[[torch.Tensor, list[int], torch.Tensor], None],
+    out_len: int,
+    device: torch.device,
+    ola: Callable[[torch.Tensor, list[int], int, int], torch.Tensor],
+    peak_limit: float = 0.9,
+    group=None,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor | None:
+    """Sharded separation of one song held in host memory (separator.py:188-201 over the ranks).
+
+    mix: (2, n) float32 on the CPU (pinned, for asynchronous copies), n >= chunk. Each rank copies only
+    the samples its shard of chunks reads, the song's peak is max-reduced over the ranks (one scalar),
+    the span is scaled by the peak gain min(1, peak_limit / peak), ``run_span(span, starts_in_span,
+    local)`` fills local[i] with the output of the chunk at span[:, s : s + chunk], the outputs are
+    gathered to rank 0, which runs the overlap-add, divides by the gain and copies the result into
+    ``out`` (if given, asynchronously) or returns it on its device. Other ranks return None.
+    """
+    rank = dist.get_rank(group)
+    world = dist.get_world_size(group)
+    n = mix.shape[1]
+    if mix.ndim != 2 or mix.shape[0] != 2 or n < chunk:
+        raise ValueError("mix must be (2, n) with n >= chunk (short clips: Separator.separate)")
+    starts = chunk_starts(n, chunk, step_for(chunk, overlap))
+    bounds = shard_bounds(len(starts), world)
+    counts = [hi - lo for lo, hi in bounds]
+    lo, hi = bounds[rank]
+    a, b = shard_span(starts, chunk, lo, hi)
+    span = torch.empty(2, b - a, device=device, dtype=torch.float32)
+    for c in range(2):  # one contiguous copy per channel row
+        span[c].copy_(mix[c, a:b], non_blocking=True)
+    peak = span.abs().amax() if b > a else torch.zeros((), device=device)
+    dist.all_reduce(peak, op=dist.ReduceOp.MAX, group=group)
+    gain = torch.where(peak > peak_limit, (peak_limit / peak.double()).float(), torch.ones((), device=device))
+    span.mul_(gain)
+    local = torch.zeros(max(counts), 2, out_len, device=device, dtype=torch.float32)
+    if hi > lo:
+        run_span(span, [s - a for s in starts[lo:hi]], local)
+    allc = gather_chunks(local, counts, group)
+    if rank != 0:
+        return None
+    inst = ola(allc, starts, chunk, n).div_(gain)
+    if out is None:
+        return inst
+    out.copy_(inst, non_blocking=True)
+    return out
+
+
 def ola_torch(chunks: torch.Tensor, starts: list[int], C: int, n: int) -> torch.Tensor:
     """Overlap-add in torch (any device), start order, used by the CPU (gloo) path."""
     w = torch.from_numpy(hamming(C)).to(chunks.device)
@@ -106,3 +162,20 @@ def separate_song_cuda(sep, x: torch.Tensor, overlap: float = 2.0, group=None,
 
     return separate_sharded(run_shard, x.shape[1], sep.chunk, overlap, model.output_length(C), x.device,
                             lambda ch, st, c, n: ola_device(ch, st, c, n), group)
+
+
+def separate_song_from_host(sep, mix: torch.Tensor, overlap: float = 2.0, out: torch.Tensor | None = None,
+                            group=None) -> torch.Tensor | None:
+    """``separate_from_host`` with the ranks' CUDA models: mix (2, n) pinned float32 on the CPU, n >= the
+    Separator's chunk; rank 0 gets the (2, n) instrumental (in ``out``, pinned, when given). Work is
+    queued without a host synchronisation; ``sep.net.check()`` reports device-side errors."""
+    from .chunking import ola_device, run_chunks
+
+    model = sep.net
+    C = sep.chunk
+
+    def run_span(span, starts, local):
+        run_chunks(model, span, starts, C, sep.batch, local, check=False)
+
+    return separate_from_host(mix, C, overlap, run_span, model.output_length(C), model.device,
+                              lambda ch, st, c, n: ola_device(ch, st, c, n), group=group, out=out)
