@@ -13,8 +13,12 @@
 //   * The running row maximum is only raised when a tile's maximum exceeds it by more than 2^8 (then O
 //     and the row sum are rescaled in place); P <= 2^8 keeps 16-bit P exact enough and the final O / l
 //     is the exact softmax average.
-//   * Each query tile has its own MMA-issuing thread (warps 1 and 10), so the two tiles' products are
+//   * Each query tile has its own MMA-issuing thread (warps 1 and 2), so the two tiles' products are
 //     issued independently: next S once the softmax has taken the previous one, P V once P is written.
+//   * At head dim 64 the exponentials, not the products, set the pace (16 ex2 per clock per SM on the
+//     MUFU pipe against 8192 tensor flops): one key pair in four is exponentiated by a polynomial on the
+//     FMA pipe instead (ex2_poly2), and the softmax warps take the registers the TMA / MMA warps do not
+//     need (setmaxnreg), so the whole score row and its packed P fit without spills.
 //   * Persistent CTAs walk the work items; Q is double buffered so the next item's first products
 //     start while the current item's epilogue runs.
 //
@@ -24,8 +28,9 @@
 //   freq mode (mode 1): sequences = (batch, frame, head), L = bands <= 64; a query tile holds two
 //                       sequences (block-diagonal mask), an item = four sequences, each tile has its own
 //                       single key tile.
-// Roles (352 threads): warp 0 TMA, warp 1 MMA issuer of tile A + TMEM owner, warps 2-5 softmax +
-// epilogue of tile A, warps 6-9 of tile B (thread = query row), warp 10 MMA issuer of tile B.
+// Roles (384 threads, three warpgroups): warp 0 TMA, warp 1 MMA issuer of tile A + TMEM owner, warp 2 MMA
+// issuer of tile B, warp 3 idle (warps 0-3 release registers); warps 4-7 softmax + epilogue of tile A,
+// warps 8-11 of tile B (thread = query row; warp w reads TMEM lanes 32 (w % 4) ..).
 #pragma once
 
 #include "gemm.cuh"  // store32
@@ -33,7 +38,13 @@
 
 namespace trc {
 
-constexpr int kAttnThreads = 352;
+constexpr int kAttnThreads = 384;
+// Time mode: registers per thread after setmaxnreg for warps 0-3 and for the softmax warpgroups. The
+// launch gives every thread the same count R (168 at 384 threads); the split needs
+// 4 * 32 * kAttnRegsLow + 8 * 32 * kAttnRegsHigh <= 384 * R, or the increase would wait forever
+// (launch_attention checks R before every time-mode launch).
+constexpr int kAttnRegsLow = 56;
+constexpr int kAttnRegsHigh = 216;
 // Key/value stages. Frequency mode loads one stage per tile and item (tile A, tile B, tile A, ...): with an
 // even stage count, stage (2 item + tile) % kAttnKvStages is only ever used by that one tile, so each
 // tile's MMA issuer waits on every phase of its stages in order. With an odd count the tiles would share
@@ -71,6 +82,25 @@ __device__ __forceinline__ uint32_t tmem_col_s(int x) { return (uint32_t)x * 128
 __device__ __forceinline__ uint32_t tmem_col_p(int x) { return 256u + (uint32_t)x * 64u; }
 __device__ __forceinline__ uint32_t tmem_col_o(int x) { return 384u + (uint32_t)x * 64u; }
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: P stays <= 2^8
+
+// 2^x for a pair of fp32 values on the FMA pipe (no MUFU): x = j + f with j = round(x) (the 1.5 * 2^23
+// rounding constant), 2^f on [-1/2, 1/2] by a degree-3 polynomial fitted here for minimum relative error
+// (Chebyshev-node least squares with Lawson reweighting; max relative error 7.5e-5, below half an fp16
+// ulp), and j added to the exponent field. x is clamped at -126 so the exponent field never wraps; the
+// inputs here are <= 2^8 and results below 2^-24 flush to zero in the 16-bit P anyway.
+__device__ __forceinline__ float2 ex2_poly2(float2 x) {
+  x = make_float2(fmaxf(x.x, -126.f), fmaxf(x.y, -126.f));
+  const float2 round_c = make_float2(12582912.0f, 12582912.0f);
+  const float2 t = __fadd2_rn(x, round_c);
+  const float2 j = __fadd2_rn(t, make_float2(-12582912.0f, -12582912.0f));
+  const float2 f = __fadd2_rn(x, make_float2(-j.x, -j.y));
+  float2 p = __ffma2_rn(make_float2(0.0551716648f, 0.0551716648f), f, make_float2(0.2426111251f, 0.2426111251f));
+  p = __ffma2_rn(p, f, make_float2(0.6932609677f, 0.6932609677f));
+  p = __ffma2_rn(p, f, make_float2(0.9999280572f, 0.9999280572f));
+  // the low mantissa bits of t hold j: shifted into the exponent field they multiply p by 2^j
+  return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
+                     __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
+}
 
 // kFreq: frequency mode (compiled separately, so each mode gets its own register allocation); it must
 // equal args.mode == 1.
@@ -133,6 +163,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
+  if (warp < 4) {
+  if constexpr (!kFreq) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kAttnRegsLow) : "memory");
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
@@ -189,7 +221,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         while (!mbar_try_wait(&q_full[k & 1], (uint32_t)(k >> 1) & 1) && global_ns() - t0 < kWaitLimitNs) {
         }
     }
-  } else if (warp == 1 || warp == kAttnThreads / 32 - 1) {
+  } else if (warp == 1 || warp == 2) {
     // ------------------------------------------------------------------ MMA issuers, one per query tile
     if (lane == 0) {
       const int x = warp == 1 ? 0 : 1;
@@ -255,9 +287,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       while (!mbar_try_wait(drain, 0) && global_ns() - t0 < kWaitLimitNs) {
       }
     }
+  }
   } else {
-    // ------------------------------------------------------------------ softmax + epilogue (warps 2-9)
-    const int x = (warp - 2) >> 2;  // query tile of this warpgroup
+    if constexpr (!kFreq) asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kAttnRegsHigh) : "memory");
+    // ------------------------------------------------------------------ softmax + epilogue (warps 4-11)
+    const int x = (warp - 4) >> 2;  // query tile of this warpgroup
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;  // query row within the tile
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
@@ -420,7 +454,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             m_run = m_tile;
           }
         }
-        // P = 2^(s log2e - m_run) as 16-bit pairs, 32 keys at a time
+        // P = 2^(s log2e - m_run) as 16-bit pairs, 32 keys at a time; the last pair of every four on the
+        // FMA pipe
         const float2 scale2 = make_float2(kLog2e, kLog2e);
         const float2 shift2 = make_float2(-m_run, -m_run);
         float2 l2 = make_float2(0.f, 0.f);
@@ -429,7 +464,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           for (int i = 0; i < 32; i += 2) {
             const int k = c * 32 + i;
             const float2 xv = __ffma2_rn(make_float2(sc[k], sc[k + 1]), scale2, shift2);
-            const float2 pv = make_float2(ex2_approx(xv.x), ex2_approx(xv.y));
+            const float2 pv = (i & 7) == 6 ? ex2_poly2(xv) : make_float2(ex2_approx(xv.x), ex2_approx(xv.y));
             l2 = __fadd2_rn(l2, pv);
             packed[i >> 1] = OperandType<TIn>::pack2(pv.x, pv.y);
           }

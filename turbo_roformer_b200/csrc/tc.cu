@@ -62,6 +62,17 @@ cudaError_t launch_attention_m(const CUtensorMap& mq, const CUtensorMap& mk, con
   static std::atomic<unsigned long long> done{0};  // one per <T, kFreq> instantiation
   cudaError_t e = allow_smem(kern, AttnSmem::kBytes, done);
   if (e != cudaSuccess) return e;
+  if (!kFreq) {
+    // the time-mode kernel moves registers between its warpgroups (setmaxnreg): the split must fit in
+    // what the launch gives the block, or the softmax warps' increase would never be granted
+    static std::atomic<int> regs{0};
+    if (regs.load() == 0) {
+      cudaFuncAttributes fa;
+      if ((e = cudaFuncGetAttributes(&fa, kern)) != cudaSuccess) return e;
+      regs.store(fa.numRegs);
+    }
+    if (4 * 32 * kAttnRegsLow + 8 * 32 * kAttnRegsHigh > kAttnThreads * regs.load()) return cudaErrorInvalidConfiguration;
+  }
   if (args.num_items <= 0) return cudaSuccess;
   const int grid = args.num_items < num_sms ? args.num_items : num_sms;
   kern<<<grid, kAttnThreads, AttnSmem::kBytes, st>>>(mq, mk, mv, args);
