@@ -77,15 +77,28 @@ def test_stft_matches_oracle(tiny_cuda, tiny_cfg, B, n):
     assert snr_db(xin_ref.numpy(), xin.cpu().numpy()) >= 100.0
 
 
-def test_band_split_matches_oracle(tiny_cuda, tiny_cfg, tiny_sd):
-    B, T = 2, 77
-    g = torch.Generator().manual_seed(1)
-    xin = torch.randn(B, T, 4 * tiny_cfg.n_freqs, generator=g)
+@pytest.mark.parametrize("B,T", [(2, 77), (1, 300)])
+def test_band_split_matches_oracle(tiny_cuda, tiny_cfg, tiny_sd, B, T):
+    """Band split as one grouped tensor-core GEMM over the bands: each band's inputs are L2-normalised
+    and rounded to fp16, the folded weights are fp16, accumulation is fp32; held to the 16-bit stages'
+    50 dB against the fp32 oracle (and against fp32 math on the same rounded operands it is exact to
+    accumulation order)."""
+    g = torch.Generator().manual_seed(1 + T)
+    xin = torch.randn(B, T, 4 * tiny_cfg.n_freqs, generator=g) * torch.logspace(-3, 1, 4 * tiny_cfg.n_freqs)
     ref = R.band_split(xin, tiny_sd, tiny_cfg).reshape(B * T * tiny_cfg.n_bands, 256)
     X = torch.empty(B * T * tiny_cfg.n_bands, 256, device="cuda")
     xin_d = xin.cuda()
     call(tiny_cuda, "trc_band_split", vp(xin_d), B, T, vp(X), stream(tiny_cuda))
-    assert snr_db(ref.numpy(), X.cpu().numpy()) >= 100.0
+    assert snr_db(ref.numpy(), X.cpu().numpy()) >= 50.0
+    # fp32 math on the fp16-rounded normalised inputs and weights: only the accumulation order differs
+    parts, outs = xin.split(tiny_cfg.band_dims, dim=-1), []
+    for k, part in enumerate(parts):
+        p = f"band_split.to_features.{k}."
+        xn = (part / part.norm(dim=-1, keepdim=True).clamp_min(1e-12)).half().float()
+        w = (tiny_sd[p + "1.weight"] * (part.shape[-1] ** 0.5) * tiny_sd[p + "0.gamma"][None, :]).half().float()
+        outs.append(xn @ w.T + tiny_sd[p + "1.bias"])
+    ref16 = torch.stack(outs, dim=-2).reshape(B * T * tiny_cfg.n_bands, 256)
+    assert snr_db(ref16.numpy(), X.cpu().numpy()) >= 100.0
 
 
 def test_add_rmsnorm(tiny_cuda):

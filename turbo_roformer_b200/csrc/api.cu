@@ -187,8 +187,13 @@ struct trc_handle {
   std::vector<std::unique_ptr<LayerDev>> layers;
   std::vector<float> rot_freqs[2];
   std::map<std::pair<int, int>, std::unique_ptr<Tables>> tables;
-  DevBuf<float> bs_wt, bs_bias;
-  DevBuf<int> bs_off;
+  // band split as a grouped GEMM: W' [256][bs_kp] 16-bit, band k in columns [pad_off[k], pad_off[k+1])
+  DevBuf<uint16_t> bs_w;
+  DevBuf<float> bs_bias;         // [nb][256]
+  DevBuf<int> bs_off, bs_poff;   // band_off, pad_off (nb + 1 each)
+  std::vector<int> pad_off;      // prefix of the band widths rounded up to 64 columns
+  int bs_kp = 0;
+  CUtensorMap m_bs_w;
   DevBuf<uint16_t> mk_w1, mk_w2;
   DevBuf<float> mk_b1, mk_b2;
   CUtensorMap m_mk_w1, m_mk_w2;
@@ -198,6 +203,7 @@ struct trc_handle {
   // forward work buffers (sized for ws_B x ws_T)
   int ws_B = 0, ws_T = 0;
   DevBuf<float> xin, X, mask, frames;
+  DevBuf<uint16_t> bs_a;  // normalised, padded band inputs [rows][bs_kp]
   DevBuf<uint16_t> xn, Q, K, V, O, H;
   DevBuf<float> G;
   // tensor maps by (pointer, precision, rank, dims, strides, box): work buffers are stable, so most hit
@@ -360,7 +366,8 @@ int ensure_workspace(trc_handle* h, int B, int T) {
   if ((rc = h->xin.alloc(BT * h->width)) || (rc = h->mask.alloc(BT * h->width)) ||
       (rc = h->frames.alloc(BT * 2 * h->n_fft)) || (rc = h->X.alloc(N * 256)) || (rc = h->xn.alloc(N * 256)) ||
       (rc = h->Q.alloc(N * 512)) || (rc = h->K.alloc(N * 512)) || (rc = h->V.alloc(N * 512)) ||
-      (rc = h->O.alloc(N * 512)) || (rc = h->H.alloc(N * hid)) || (rc = h->G.alloc(N * 8)))
+      (rc = h->O.alloc(N * 512)) || (rc = h->H.alloc(N * hid)) || (rc = h->G.alloc(N * 8)) ||
+      (rc = h->bs_a.alloc(BT * h->bs_kp)))
     return rc;
   h->ws_B = nB;
   h->ws_T = nT;
@@ -643,17 +650,57 @@ int run_mask(trc_handle* h, const void* xn, int B, int T, float* mask, void* hid
 
 int frames_for(const trc_handle* h, int64_t samples) { return (int)(1 + samples / h->hop); }
 
+// Band split (model.py:147-155) + the transformers' first norm: the band-pack kernel normalises and pads
+// each band's inputs into h->bs_a (16-bit), then one grouped GEMM over the bands writes X = A W'^T + b
+// [rows][nb][256] fp32 and xn = X / max(|X|, 1e-12) (16-bit).
+int run_band_split(trc_handle* h, const float* xin, int B, int T, float* X, void* xn, cudaStream_t st) {
+  const int rows = B * T;
+  const int nb = h->nb;
+  trc::launch_band_pack(xin, h->width, rows, nb, h->bs_off.p, h->bs_poff.p, h->bs_kp, h->bs_a.p, h->prec, st);
+  int rc;
+  if ((rc = check_launch(cudaGetLastError(), "band pack"))) return rc;
+  CUtensorMap ma;
+  if ((rc = map_2d_cached(h, &ma, h->bs_a.p, h->bs_kp, rows, 128))) return rc;
+  const CUtensorMap mo[3] = {ma, ma, ma};  // the epilogue stores directly
+  GemmArgs a;
+  std::memset(&a, 0, sizeof(a));
+  a.a_mode = trc::A_BAND;
+  a.M = rows;
+  a.F = nb;
+  a.n_groups = nb;
+  const int mt = (rows + 127) / 128;
+  for (int g = 0; g < nb; ++g) {
+    a.g_tile_start[g] = g * mt;
+    a.g_ntiles[g] = 1;
+    a.g_brow[g] = 0;
+    a.g_ncols[g] = 256;
+    a.g_koff[g] = h->pad_off[g];
+    a.g_kblocks[g] = (h->pad_off[g + 1] - h->pad_off[g]) / 64;
+  }
+  a.g_tile_start[nb] = nb * mt;
+  a.num_tiles = nb * mt;
+  a.out0 = X;
+  a.out1 = xn;
+  a.bias = h->bs_bias.p;
+  a.eps = 1e-12f;
+  a.err = h->err.p;
+  return check_launch(trc::launch_gemm(trc::EPI_BAND, h->prec, ma, h->m_bs_w, mo, a, h->num_sms, st), "band split");
+}
+
 // The 2*depth transformers of fast.py:269-341 on the residual stream X [batch*T*bands][256] fp32 (updated
 // in place): the first norm, then per transformer qkv + rotary, attention, out-projection + residual +
-// norm, feed-forward + residual + norm. The last normalised stream is left in h->xn (the mask's input).
-int run_transformers(trc_handle* h, float* X, int batch, int T, cudaStream_t st) {
+// norm, feed-forward + residual + norm (xn_ready: h->xn already holds the first norm). The last normalised
+// stream is left in h->xn (the mask's input).
+int run_transformers(trc_handle* h, float* X, int batch, int T, cudaStream_t st, bool xn_ready) {
   const int64_t rows = (int64_t)batch * T * h->nb;
   int rc;
-  {
-    Section sec(h, "norm", st);
-    trc::launch_rownorm(X, h->xn.p, rows, 1e-12f, h->prec, st);
+  if (!xn_ready) {
+    {
+      Section sec(h, "norm", st);
+      trc::launch_rownorm(X, h->xn.p, rows, 1e-12f, h->prec, st);
+    }
+    if ((rc = check_launch(cudaGetLastError(), "norm"))) return rc;
   }
-  if ((rc = check_launch(cudaGetLastError(), "norm"))) return rc;
   for (int l = 0; l < 2 * h->depth; ++l) {
     const int mode = l & 1;
     {
@@ -799,10 +846,15 @@ int trc_prepare(trc_handle* h) {
       h->layers.push_back(std::move(L));
     }
   }
-  // band split (model.py:147-155): W'^T [sum din][256] with sqrt(din) * gamma folded, bias [nb][256]
+  // band split (model.py:147-155) as one grouped GEMM over the bands: W' [256][bs_kp] 16-bit with the
+  // RMSNorm gain sqrt(din) * gamma folded in, band k in columns [pad_off[k], pad_off[k] + din) and zeros
+  // up to the next multiple of 64; bias [nb][256]
   {
-    const int W = h->band_off[h->nb];
-    std::vector<float> wt((size_t)W * d), bias((size_t)h->nb * d);
+    h->pad_off.assign(h->nb + 1, 0);
+    for (int k = 0; k < h->nb; ++k) h->pad_off[k + 1] = h->pad_off[k] + (4 * h->freqs[k] + 63) / 64 * 64;
+    h->bs_kp = h->pad_off[h->nb];
+    const int kp = h->bs_kp;
+    std::vector<float> w((size_t)d * kp, 0.f), bias((size_t)h->nb * d);
     for (int k = 0; k < h->nb; ++k) {
       const int din = 4 * h->freqs[k];
       const std::string p = "band_split.to_features." + std::to_string(k) + ".";
@@ -811,13 +863,12 @@ int trc_prepare(trc_handle* h) {
       const auto* bk = param(h, p + "1.bias", d);
       if (!gk || !wk || !bk) return TRC_E_INVALID;
       const float sc = (float)std::sqrt((double)din);
-      for (int c = 0; c < din; ++c) {
-        const float gc = sc * (*gk)[c];
-        for (int o = 0; o < d; ++o) wt[(size_t)(h->band_off[k] + c) * d + o] = (*wk)[(size_t)o * din + c] * gc;
-      }
+      for (int o = 0; o < d; ++o)
+        for (int c = 0; c < din; ++c) w[(size_t)o * kp + h->pad_off[k] + c] = (*wk)[(size_t)o * din + c] * (sc * (*gk)[c]);
       for (int o = 0; o < d; ++o) bias[(size_t)k * d + o] = (*bk)[o];
     }
-    if ((rc = h->bs_wt.upload(wt)) || (rc = h->bs_bias.upload(bias)) || (rc = h->bs_off.upload(h->band_off)))
+    if ((rc = upload_bits(h->bs_w, w, prec)) || (rc = h->bs_bias.upload(bias)) || (rc = h->bs_off.upload(h->band_off)) ||
+        (rc = h->bs_poff.upload(h->pad_off)) || (rc = map_2d(&h->m_bs_w, prec, h->bs_w.p, kp, d, 256)))
       return rc;
   }
   // mask estimator (model.py:158-178; fast.py:140-160, 385-386): final gain folded into layer 1,
@@ -938,12 +989,12 @@ int trc_forward(trc_handle* h, const float* d_audio, int batch, int64_t samples,
     Section sec(h, "stft", st);
     trc::launch_stft(d_audio, batch, samples, T, h->n_fft, h->hop, h->window.p, h->tw_fwd.p, h->xin.p, st);
   }
+  if ((rc = check_launch(cudaGetLastError(), "stft"))) return rc;
   {
-    Section sec(h, "band_split", st);
-    trc::launch_band_split(h->xin.p, h->width, batch * T, h->nb, h->bs_off.p, h->bs_wt.p, h->bs_bias.p, h->X.p, st);
+    Section sec(h, "band_split", st, 2);
+    if ((rc = run_band_split(h, h->xin.p, batch, T, h->X.p, h->xn.p, st))) return rc;
   }
-  if ((rc = check_launch(cudaGetLastError(), "stft/band split"))) return rc;
-  if ((rc = run_transformers(h, h->X.p, batch, T, st))) return rc;
+  if ((rc = run_transformers(h, h->X.p, batch, T, st, true))) return rc;
   {
     Section sec(h, "mask", st, 2);
     if ((rc = run_mask(h, h->xn.p, batch, T, h->mask.p, h->H.p, st))) return rc;
@@ -962,7 +1013,7 @@ int trc_transformer(trc_handle* h, float* d_X, int batch, int T, void* stream) {
   if ((int64_t)batch * T * h->nb >= (1ll << 31) / 512) return fail(TRC_E_INVALID, "batch too large");
   int rc;
   if ((rc = ensure_workspace(h, batch, T))) return rc;
-  return run_transformers(h, d_X, batch, T, (cudaStream_t)stream);
+  return run_transformers(h, d_X, batch, T, (cudaStream_t)stream, false);
 }
 
 int trc_profile(trc_handle* h, int enable) {
@@ -1151,11 +1202,12 @@ int trc_stft(trc_handle* h, const float* d_audio, int batch, int64_t samples, fl
 
 int trc_band_split(trc_handle* h, const float* d_xin, int batch, int T, float* d_X, void* stream) {
   TRC_REQUIRE_PREPARED(h);
-  if (batch < 1 || T < 1) return fail(TRC_E_INVALID, "bad band_split arguments");
-  Section sec(h, "band_split", (cudaStream_t)stream);
-  trc::launch_band_split(d_xin, h->width, batch * T, h->nb, h->bs_off.p, h->bs_wt.p, h->bs_bias.p, d_X,
-                         (cudaStream_t)stream);
-  return check_launch(cudaGetLastError(), "band_split");
+  if (!d_xin || !d_X || batch < 1 || T < 1) return fail(TRC_E_INVALID, "bad band_split arguments");
+  if ((int64_t)batch * T * h->nb >= (1ll << 31) / 512) return fail(TRC_E_INVALID, "batch too large");
+  int rc;
+  if ((rc = ensure_workspace(h, batch, T))) return rc;
+  Section sec(h, "band_split", (cudaStream_t)stream, 2);
+  return run_band_split(h, d_xin, batch, T, d_X, h->xn.p, (cudaStream_t)stream);
 }
 
 int trc_mask(trc_handle* h, const void* d_xn, int batch, int T, float* d_mask, void* d_hidden, void* stream) {

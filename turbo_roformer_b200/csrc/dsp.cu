@@ -14,18 +14,45 @@ namespace trc {
 // ------------------------------------------------------------------------------------------------ FFT
 // In-place iterative radix-2 FFT of N = 2^log2n complex values in shared memory that were stored in
 // bit-reversed order. tw[k] = exp(sign * 2 pi i k / N), k < N/2 (computed on the host in fp64).
+// Two consecutive radix-2 stages (s and s + 1) are done as one radix-4 pass: each thread takes the four
+// values a stage-s butterfly pair and its partner pair feed into, so every value is read and written
+// once per two stages and the block synchronises half as often. The arithmetic per output is the
+// radix-2 stages' own.
+__device__ __forceinline__ float2 cmul(float2 b, float2 w) {
+  return make_float2(b.x * w.x - b.y * w.y, b.x * w.y + b.y * w.x);
+}
+
 __device__ __forceinline__ void fft_smem(float2* buf, const float2* __restrict__ tw, int n, int log2n) {
-  for (int s = 1; s <= log2n; ++s) {
+  int s = 1;
+  for (; s + 1 <= log2n; s += 2) {
+    const int h = 1 << (s - 1);  // stage-s butterfly distance; stage s + 1 uses 2h
+    for (int j = threadIdx.x; j < (n >> 2); j += blockDim.x) {
+      const int pos = j & (h - 1);
+      const int i0 = ((j >> (s - 1)) << (s + 1)) + pos;
+      const float2 w1 = __ldg(&tw[pos * (n >> s)]);             // W_{2h}^pos
+      const float2 w2 = __ldg(&tw[pos * (n >> (s + 1))]);       // W_{4h}^pos
+      const float2 w3 = __ldg(&tw[(pos + h) * (n >> (s + 1))]);  // W_{4h}^(pos + h)
+      const float2 a = buf[i0], b = buf[i0 + h], c = buf[i0 + 2 * h], d = buf[i0 + 3 * h];
+      const float2 bw = cmul(b, w1), dw = cmul(d, w1);
+      const float2 a1 = make_float2(a.x + bw.x, a.y + bw.y), b1 = make_float2(a.x - bw.x, a.y - bw.y);
+      const float2 c1 = make_float2(c.x + dw.x, c.y + dw.y), d1 = make_float2(c.x - dw.x, c.y - dw.y);
+      const float2 cw = cmul(c1, w2), dw2 = cmul(d1, w3);
+      buf[i0] = make_float2(a1.x + cw.x, a1.y + cw.y);
+      buf[i0 + 2 * h] = make_float2(a1.x - cw.x, a1.y - cw.y);
+      buf[i0 + h] = make_float2(b1.x + dw2.x, b1.y + dw2.y);
+      buf[i0 + 3 * h] = make_float2(b1.x - dw2.x, b1.y - dw2.y);
+    }
+    __syncthreads();
+  }
+  if (s == log2n) {  // odd number of stages: a last radix-2 stage
     const int half = 1 << (s - 1);
-    const int tstride = n >> s;
     for (int j = threadIdx.x; j < (n >> 1); j += blockDim.x) {
       const int pos = j & (half - 1);
       const int i0 = ((j >> (s - 1)) << s) + pos;
       const int i1 = i0 + half;
-      const float2 w = __ldg(&tw[pos * tstride]);
+      const float2 w = __ldg(&tw[pos * (n >> s)]);
       const float2 a = buf[i0];
-      const float2 b = buf[i1];
-      const float2 bw = make_float2(b.x * w.x - b.y * w.y, b.x * w.y + b.y * w.x);
+      const float2 bw = cmul(buf[i1], w);
       buf[i0] = make_float2(a.x + bw.x, a.y + bw.y);
       buf[i1] = make_float2(a.x - bw.x, a.y - bw.y);
     }
@@ -128,63 +155,33 @@ __global__ void istft_ola_kernel(const float* __restrict__ frames, int B, int T,
   out[(size_t)b * 2 * lout + lout + i] = s1 / env;
 }
 
-// Band split (turbo_roformer/model.py:147-155): per band k, X = W'_k x / max(|x|, 1e-12) + b_k with the
-// RMSNorm gain sqrt(din) * gamma folded into W'. One block = 64 rows (batch x frame) of one band;
-// thread o = output feature. wt [sum din][256] (transposed, folded), bias [nbands][256],
-// X [rows][nbands][256] fp32.
-// R rows (frames) x one band x 256 outputs per block: a thread owns one output column for R rows; small R
-// gives many short blocks, which balances the very different band widths (8 to 512 inputs) over the SMs.
-template <int R>
-__global__ void __launch_bounds__(256) band_split_kernel(const float* __restrict__ xin, int width, int rows,
-                                                         int nbands, const int* __restrict__ band_off,
-                                                         const float* __restrict__ wt, const float* __restrict__ bias,
-                                                         float* __restrict__ X) {
-  __shared__ __align__(16) float xs[R][68];  // row stride 68 keeps float4 reads 16-byte aligned
-  __shared__ float ssq_s[R];
-  const int band = blockIdx.y;
-  const int r0 = blockIdx.x * R;
-  const int off = band_off[band];
-  const int din = band_off[band + 1] - off;  // 4 * bins: always a multiple of 4
-  const int o = threadIdx.x;
-  float acc[R];
+// Band-split inputs of one frame for the grouped band-split GEMM (turbo_roformer/model.py:147-155): each
+// band's 4 * bins values divided by their L2 norm (F.normalize inside the band's RMSNorm, eps 1e-12; the
+// sqrt(din) * gamma gain is folded into the GEMM's weights), rounded to the operand type, each band
+// starting at a multiple of 64 columns and zero-padded up to the next one.
+// xin [rows][width] fp32 (band k at columns band_off[k] ..); a [rows][kp] 16-bit (band k at pad_off[k]).
+// One block per frame; its warps take the bands in turn.
+template <typename TOut>
+__global__ void __launch_bounds__(256) band_pack_kernel(const float* __restrict__ xin, int width, int nbands,
+                                                        const int* __restrict__ band_off,
+                                                        const int* __restrict__ pad_off, int kp,
+                                                        TOut* __restrict__ a) {
+  const int row = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float* x = xin + (size_t)row * width;
+  TOut* o = a + (size_t)row * kp;
+  for (int k = warp; k < nbands; k += blockDim.x >> 5) {
+    const int off = band_off[k], din = band_off[k + 1] - off;
+    const int po = pad_off[k], pw = pad_off[k + 1] - po;
+    float ss = 0.f;
+    for (int c = lane; c < din; c += 32) {
+      const float v = x[off + c];
+      ss = fmaf(v, v, ss);
+    }
 #pragma unroll
-  for (int r = 0; r < R; ++r) acc[r] = 0.f;
-  float ssq = 0.f;
-  for (int c0 = 0; c0 < din; c0 += 64) {
-    const int cw = min(64, din - c0);
-#pragma unroll 4
-    for (int k = 0; k < R / 4; ++k) {
-      const int e = o + k * 256;
-      const int row = e >> 6, col = e & 63;
-      float v = 0.f;
-      if (r0 + row < rows && col < cw) v = xin[(size_t)(r0 + row) * width + off + c0 + col];
-      xs[row][col] = v;
-    }
-    __syncthreads();
-    if (o < R) {
-      for (int col = 0; col < cw; ++col) ssq += xs[o][col] * xs[o][col];
-    }
-    for (int i = 0; i < cw; i += 4) {
-      const float* wp = wt + (size_t)(off + c0 + i) * 256 + o;
-      const float w0 = wp[0], w1 = wp[256], w2 = wp[512], w3 = wp[768];
-#pragma unroll
-      for (int r = 0; r < R; ++r) {
-        const float4 xv = *reinterpret_cast<const float4*>(&xs[r][i]);
-        acc[r] = fmaf(xv.w, w3, fmaf(xv.z, w2, fmaf(xv.y, w1, fmaf(xv.x, w0, acc[r]))));
-      }
-    }
-    __syncthreads();
-  }
-  if (o < R) ssq_s[o] = ssq;
-  __syncthreads();
-  const float bo = bias[band * 256 + o];
-#pragma unroll 4
-  for (int r = 0; r < R; ++r) {
-    const int row = r0 + r;
-    if (row < rows) {
-      const float inv = 1.0f / fmaxf(sqrtf(ssq_s[r]), 1e-12f);
-      X[((size_t)row * nbands + band) * 256 + o] = acc[r] * inv + bo;
-    }
+    for (int d = 16; d > 0; d >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, d);
+    const float inv = 1.0f / fmaxf(sqrtf(ss), 1e-12f);
+    for (int c = lane; c < pw; c += 32) o[po + c] = OperandType<TOut>::from_float(c < din ? x[off + c] * inv : 0.f);
   }
 }
 
@@ -247,40 +244,54 @@ __global__ void add_rmsnorm_kernel(float* __restrict__ X, const float* __restric
 // with separately rounded multiply and add, so the result equals the reference's sequential
 // `result += y * w; weight += w; result / max(weight, 1e-10)` bit for bit.
 // chunks [n_chunks][2][clen]; out [2][n].
-__global__ void chunk_ola_kernel(const float* __restrict__ chunks, int64_t clen, const int64_t* __restrict__ starts,
-                                 int n_chunks, const float* __restrict__ w, int64_t n, float* __restrict__ out) {
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= n) return;
-  // hi = last chunk with start <= i ; lo = first chunk with start > i - clen
-  int lo = 0, hi = n_chunks - 1;
-  {
+// A block owns kOlaPerThread consecutive samples per thread, laid out block-strided (sample
+// i0 + s * blockDim.x + threadIdx.x for s < kOlaPerThread) so every load and store stays coalesced; one
+// pair of binary searches per block finds the chunks that cover the block's span, and each sample then
+// walks that short range, skipping chunks that do not cover it.
+constexpr int kOlaPerThread = 8;
+
+__global__ void __launch_bounds__(256) chunk_ola_kernel(const float* __restrict__ chunks, int64_t clen,
+                                                        const int64_t* __restrict__ starts, int n_chunks,
+                                                        const float* __restrict__ w, int64_t n,
+                                                        float* __restrict__ out) {
+  __shared__ int range[2];
+  const int64_t i0 = (int64_t)blockIdx.x * blockDim.x * kOlaPerThread;
+  const int64_t i1 = min(n, i0 + (int64_t)blockDim.x * kOlaPerThread) - 1;  // last sample of the block
+  if (threadIdx.x == 0) {
+    // hi = last chunk with start <= i1 ; lo = first chunk with start > i0 - clen
     int a = 0, b = n_chunks - 1, res = -1;
     while (a <= b) {
       const int mid = (a + b) >> 1;
-      if (starts[mid] <= i) { res = mid; a = mid + 1; } else { b = mid - 1; }
+      if (starts[mid] <= i1) { res = mid; a = mid + 1; } else { b = mid - 1; }
     }
-    hi = res;
-  }
-  {
-    int a = 0, b = n_chunks - 1, res = n_chunks;
+    range[1] = res;
+    a = 0, b = n_chunks - 1, res = n_chunks;
     while (a <= b) {
       const int mid = (a + b) >> 1;
-      if (starts[mid] > i - clen) { res = mid; b = mid - 1; } else { a = mid + 1; }
+      if (starts[mid] > i0 - clen) { res = mid; b = mid - 1; } else { a = mid + 1; }
     }
-    lo = res;
+    range[0] = res;
   }
-  float r0 = 0.f, r1 = 0.f, ws = 0.f;
-  for (int c = lo; c <= hi; ++c) {
-    const int64_t k = i - starts[c];
-    const float wv = w[k];
-    const float* y = chunks + (size_t)c * 2 * clen;
-    r0 = __fadd_rn(r0, __fmul_rn(y[k], wv));
-    r1 = __fadd_rn(r1, __fmul_rn(y[clen + k], wv));
-    ws = __fadd_rn(ws, wv);
+  __syncthreads();
+  const int lo = range[0], hi = range[1];
+#pragma unroll
+  for (int s = 0; s < kOlaPerThread; ++s) {
+    const int64_t i = i0 + (int64_t)s * blockDim.x + threadIdx.x;
+    if (i >= n) break;
+    float r0 = 0.f, r1 = 0.f, ws = 0.f;
+    for (int c = lo; c <= hi; ++c) {
+      const int64_t k = i - starts[c];
+      if (k < 0 || k >= clen) continue;  // chunk c does not cover sample i
+      const float wv = w[k];
+      const float* y = chunks + (size_t)c * 2 * clen;
+      r0 = __fadd_rn(r0, __fmul_rn(y[k], wv));
+      r1 = __fadd_rn(r1, __fmul_rn(y[clen + k], wv));
+      ws = __fadd_rn(ws, wv);
+    }
+    const float d = fmaxf(ws, 1e-10f);
+    out[i] = __fdiv_rn(r0, d);
+    out[n + i] = __fdiv_rn(r1, d);
   }
-  const float d = fmaxf(ws, 1e-10f);
-  out[i] = __fdiv_rn(r0, d);
-  out[n + i] = __fdiv_rn(r1, d);
 }
 
 // ------------------------------------------------------------------------------------------------ launchers
@@ -299,10 +310,13 @@ void launch_istft(const float* xin, const float* mask, int B, int T, int n, int 
   istft_ola_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(frames, B, T, n, hop, window, out, lout);
 }
 
-void launch_band_split(const float* xin, int width, int rows, int nbands, const int* band_off, const float* wt,
-                       const float* bias, float* X, cudaStream_t st) {
-  dim3 grid((rows + 15) / 16, nbands);
-  band_split_kernel<16><<<grid, 256, 0, st>>>(xin, width, rows, nbands, band_off, wt, bias, X);
+void launch_band_pack(const float* xin, int width, int rows, int nbands, const int* band_off, const int* pad_off,
+                      int kp, void* a, int precision, cudaStream_t st) {
+  if (precision == 0)
+    band_pack_kernel<__half><<<rows, 256, 0, st>>>(xin, width, nbands, band_off, pad_off, kp, static_cast<__half*>(a));
+  else
+    band_pack_kernel<__nv_bfloat16>
+        <<<rows, 256, 0, st>>>(xin, width, nbands, band_off, pad_off, kp, static_cast<__nv_bfloat16*>(a));
 }
 
 void launch_rownorm(const float* X, void* xn, int64_t rows, float eps, int precision, cudaStream_t st) {
@@ -341,7 +355,9 @@ void launch_wait_timeout_selftest(int* err, cudaStream_t st) { wait_timeout_self
 
 void launch_chunk_ola(const float* chunks, int64_t clen, const int64_t* d_starts, int n_chunks, const float* w,
                       int64_t n, float* out, cudaStream_t st) {
-  chunk_ola_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(chunks, clen, d_starts, n_chunks, w, n, out);
+  const int64_t per_block = 256 * kOlaPerThread;
+  chunk_ola_kernel<<<(unsigned)((n + per_block - 1) / per_block), 256, 0, st>>>(chunks, clen, d_starts, n_chunks, w,
+                                                                                 n, out);
 }
 
 }  // namespace trc

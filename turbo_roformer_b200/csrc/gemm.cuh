@@ -15,13 +15,15 @@
 //   EPI_GELU      gemm_gelu (:610-642):     H = gelu(acc + b), erf by A&S 7.1.28
 //   EPI_MASK_TANH mask MLP layer 1 (fast.py:354):  tanh(acc + b1) per band
 //   EPI_MASK_GLU  mask MLP layer 2 + GLU (fast.py:355-357): a * sigmoid(g), with (a, g) rows interleaved
+//   EPI_BAND      band split (model.py:147-155): X = acc + b per band, and the transformers' first norm
+//                 xn = X / max(|X|, eps) (kernels.cpp:102-137) in the same pass
 #pragma once
 
 #include "sm100.cuh"
 
 namespace trc {
 
-enum EpiKind : int { EPI_QKV = 0, EPI_RESNORM = 1, EPI_GELU = 2, EPI_MASK_TANH = 3, EPI_MASK_GLU = 4 };
+enum EpiKind : int { EPI_QKV = 0, EPI_RESNORM = 1, EPI_GELU = 2, EPI_MASK_TANH = 3, EPI_MASK_GLU = 4, EPI_BAND = 5 };
 
 // How a tile's 128 A rows are addressed.
 enum AMode : int {
@@ -30,6 +32,7 @@ enum AMode : int {
   A_ROWS_GROUP = 2,  // 3-D (K, rows, group): group-major storage (mask layer 2)
   A_TIME_SEQ = 3,    // 4-D (K, band, frame, batch): 128 consecutive frames of one band (time qkv)
   A_FREQ_PAIR = 4,   // 3-D (K, band, frame): two frames x 64 band slots (freq qkv)
+  A_BAND = 5,        // 2-D [rows][K]: each group (band) reads its own K range (g_koff, g_kblocks)
 };
 
 constexpr int kGemmBM = 128;
@@ -56,6 +59,8 @@ struct GemmArgs {
   int g_brow[kMaxGroups];    // first B row of the group
   int g_ncols[kMaxGroups];   // valid columns of the group
   int g_outoff[kMaxGroups];  // output column offset of the group (mask GLU)
+  int g_koff[kMaxGroups];    // A_BAND: first K element of the group (a multiple of 64)
+  int g_kblocks[kMaxGroups]; // A_BAND: K blocks of the group
   // ---- epilogue
   void* out0;
   void* out1;
@@ -72,6 +77,7 @@ struct GemmArgs {
 
 struct TileCoord {
   int m0, n0, group, b_row, n_valid, n_mma;
+  int koff, kblocks;  // K range: [koff, koff + 64 * kblocks)
   int a1, a2, a3;  // TMA coordinates of A after the K coordinate
   int b, f;        // time qkv: batch item and band of the tile
 };
@@ -83,6 +89,8 @@ __device__ __forceinline__ TileCoord gemm_decode(const GemmArgs& a, int tile) {
   c.b = 0;
   c.f = 0;
   c.a3 = 0;
+  c.koff = 0;
+  c.kblocks = a.k_blocks;
   int nt;
   if (a.n_groups > 0) {
     int g = 0;
@@ -95,7 +103,12 @@ __device__ __forceinline__ TileCoord gemm_decode(const GemmArgs& a, int tile) {
     c.n0 = nt * BN;
     c.b_row = a.g_brow[g] + c.n0;
     c.n_valid = min(BN, a.g_ncols[g] - c.n0);
-    if (a.a_mode == A_GROUP_ROWS) {
+    if (a.a_mode == A_BAND) {
+      c.a1 = c.m0;
+      c.a2 = 0;
+      c.koff = a.g_koff[g];
+      c.kblocks = a.g_kblocks[g];
+    } else if (a.a_mode == A_GROUP_ROWS) {
       c.a1 = g;
       c.a2 = c.m0;
     } else {
@@ -548,6 +561,59 @@ __device__ __forceinline__ void epi_glu(const GemmArgs& a, const TileCoord& tc, 
   }
 }
 
+// Band split + first norm (EPI_BAND): each thread owns one row (frame) and one column half of the
+// band's 256 outputs. X = acc + b is written as fp32 (512 contiguous bytes per thread), the two halves
+// of a row meet in shared memory with their sums of squares, and xn = X / max(|X|, eps) is written as
+// 16-bit from a second read of the accumulator. X [rows][bands][256] fp32 (out0), xn the same in 16 bits
+// (out1). Returns false if the row-sum exchange was abandoned (a failed wait elsewhere).
+template <int BN, typename TIn>
+__device__ __forceinline__ bool epi_band(const GemmArgs& a, const TileCoord& tc, EpiCtx& e, float* rs_base,
+                                         int local_tile) {
+  static_assert(BN == 256, "the band epilogue covers whole 256-wide rows");
+  const int m = tc.m0 + e.row;
+  const bool valid = m < a.M;
+  const size_t row_off = ((size_t)m * a.F + tc.group) * 256 + e.hf * 128;
+  const float* bias = a.bias + tc.group * 256 + e.hf * 128;
+  float ss = 0.f;
+#pragma unroll 1
+  for (int c = 0; c < 4; ++c) {
+    float v[32];
+    tmem_ld32(e.taddr + e.hf * 128 + c * 32, v);
+    const float4* b4 = reinterpret_cast<const float4*>(bias + c * 32);
+    float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out0) + row_off + c * 32);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float4 b = __ldg(b4 + q);
+      const float4 x = make_float4(v[4 * q] + b.x, v[4 * q + 1] + b.y, v[4 * q + 2] + b.z, v[4 * q + 3] + b.w);
+      ss = fmaf(x.x, x.x, fmaf(x.y, x.y, fmaf(x.z, x.z, fmaf(x.w, x.w, ss))));
+      if (valid) dst[q] = x;
+    }
+  }
+  float* rs = rs_base + (local_tile & 1) * 256;
+  rs[e.hf * 128 + e.quarter * 32 + e.lane] = ss;
+  if (!named_bar_and(3, 32 * kEpiWarps, true)) return false;
+  const float tot = rs[e.quarter * 32 + e.lane] + rs[128 + e.quarter * 32 + e.lane];
+  const float inv = 1.0f / fmaxf(sqrtf(tot), a.eps);
+#pragma unroll 1
+  for (int c = 0; c < 4; ++c) {
+    float v[32];
+    tmem_ld32(e.taddr + e.hf * 128 + c * 32, v);
+    const float4* b4 = reinterpret_cast<const float4*>(bias + c * 32);
+    uint4* dst = reinterpret_cast<uint4*>(static_cast<TIn*>(a.out1) + row_off + c * 32);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float4 b0 = __ldg(b4 + 2 * q), b1 = __ldg(b4 + 2 * q + 1);
+      uint4 u;
+      u.x = OperandType<TIn>::pack2((v[8 * q] + b0.x) * inv, (v[8 * q + 1] + b0.y) * inv);
+      u.y = OperandType<TIn>::pack2((v[8 * q + 2] + b0.z) * inv, (v[8 * q + 3] + b0.w) * inv);
+      u.z = OperandType<TIn>::pack2((v[8 * q + 4] + b1.x) * inv, (v[8 * q + 5] + b1.y) * inv);
+      u.w = OperandType<TIn>::pack2((v[8 * q + 6] + b1.z) * inv, (v[8 * q + 7] + b1.w) * inv);
+      if (valid) dst[q] = u;
+    }
+  }
+  return true;
+}
+
 // ------------------------------------------------------------------------------------------------ kernel
 template <int BN, int STAGES, int EPI>
 struct GemmSmem {
@@ -563,8 +629,8 @@ struct GemmSmem {
   static constexpr int kOutBytes = 2 * kSlabsPerHalf * kSlabBytes;
   static_assert(EPI != EPI_RESNORM || kEpiWarps * 2 * kResBoxBytes <= kOutBytes, "residual-norm boxes must fit");
   static constexpr int kTabOffset = kOutOffset + kOutBytes;  // rotary rows (qkv only)
-  static constexpr int kRsOffset = kTabOffset + (EPI == EPI_QKV ? kTabBytes : 0);  // row sums (res-norm only)
-  static constexpr int kBarOffset = kRsOffset + (EPI == EPI_RESNORM ? 2 * 256 * 4 : 0);
+  static constexpr int kRsOffset = kTabOffset + (EPI == EPI_QKV ? kTabBytes : 0);  // row sums (norm epilogues)
+  static constexpr int kBarOffset = kRsOffset + (EPI == EPI_RESNORM || EPI == EPI_BAND ? 2 * 256 * 4 : 0);
   static constexpr int kBytes = kBarOffset + 256 + 1024;  // + barriers + alignment slack
   static_assert(kBytes <= 232448, "shared memory per CTA");
 };
@@ -593,7 +659,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int a_dims = args.a_mode == A_ROWS ? 2 : args.a_mode == A_TIME_SEQ ? 4 : 3;
+  const int a_dims = (args.a_mode == A_ROWS || args.a_mode == A_BAND) ? 2 : args.a_mode == A_TIME_SEQ ? 4 : 3;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -659,14 +725,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         for (int u = 0; u < tiles_per_unit && ok; ++u) {
         const TileCoord tc = gemm_decode<BN>(args, unit * tiles_per_unit + u);
-        for (int kb = 0; kb < args.k_blocks; ++kb) {
+        for (int kb = 0; kb < tc.kblocks; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, args.err, kErrWaitProducer, abort_flag)) {
             ok = false;
             break;
           }
           uint8_t* st = smem + S::kStageOffset + stage * S::kStageBytes;
           mbar_arrive_expect_tx(&full[stage], S::kStageBytes);
-          const int kx = kb * kGemmBK;
+          const int kx = tc.koff + kb * kGemmBK;
           if constexpr (S::kAStat) {
             tma_load_2d(st, &map_b, &full[stage], kx, tc.b_row);
           } else {
@@ -726,7 +792,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(buf * BN);
         const uint32_t idesc = idesc_f16(kGemmBM, tc.n_mma, OperandType<TIn>::kFormat, 0, 0);
-        for (int kb = 0; kb < args.k_blocks; ++kb) {
+        for (int kb = 0; kb < tc.kblocks; ++kb) {
           if (!mbar_wait(&full[stage], phase, args.err, kErrWaitMma, abort_flag)) {
             ok = false;
             break;
@@ -814,6 +880,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         epi_act<BN, TIn>(args, tc, e, &map_o0, false);
       } else if constexpr (EPI == EPI_MASK_TANH) {
         epi_act<BN, TIn>(args, tc, e, &map_o0, true);
+      } else if constexpr (EPI == EPI_BAND) {
+        if (!epi_band<BN, TIn>(args, tc, e, reinterpret_cast<float*>(smem + S::kRsOffset), local)) {
+          run = false;
+          break;
+        }
       } else {
         epi_glu<BN>(args, tc, e);
       }

@@ -19,8 +19,8 @@ void launch_stft(const float* audio, int B, int64_t L, int T, int n, int hop, co
                  float* xin, cudaStream_t st);
 void launch_istft(const float* xin, const float* mask, int B, int T, int n, int hop, const float* window,
                   const float2* tw_inv, float* frames, float* out, cudaStream_t st);
-void launch_band_split(const float* xin, int width, int rows, int nbands, const int* band_off, const float* wt,
-                       const float* bias, float* X, cudaStream_t st);
+void launch_band_pack(const float* xin, int width, int rows, int nbands, const int* band_off, const int* pad_off,
+                      int kp, void* a, int precision, cudaStream_t st);
 void launch_rownorm(const float* X, void* xn, int64_t rows, float eps, int precision, cudaStream_t st);
 void launch_add_rmsnorm(float* X, const float* Y, void* out, int out_f32, int64_t rows, float eps, int precision,
                         cudaStream_t st);

@@ -51,6 +51,7 @@ cudaError_t launch_gemm_p(int epi, const CUtensorMap& ma, const CUtensorMap& mb,
     case EPI_GELU: return launch_gemm_t<EPI_GELU, T>(ma, mb, mo, args, num_sms, st);
     case EPI_MASK_TANH: return launch_gemm_t<EPI_MASK_TANH, T>(ma, mb, mo, args, num_sms, st);
     case EPI_MASK_GLU: return launch_gemm_t<EPI_MASK_GLU, T>(ma, mb, mo, args, num_sms, st);
+    case EPI_BAND: return launch_gemm_t<EPI_BAND, T>(ma, mb, mo, args, num_sms, st);
     default: return cudaErrorInvalidValue;
   }
 }
