@@ -160,3 +160,27 @@ def test_service_load_overlap3(sep):
     jobs = [sep.submit(torch.from_numpy(m).pin_memory(), overlap=3.0) for m in songs]
     for r, j in zip(ref, jobs):
         np.testing.assert_array_equal(j.result(), r)
+
+
+def test_queued_songs_share_forwards(sep):
+    """Chunks of songs queued back to back share forwards (a song's last chunks fill a batch with the
+    next song's first ones): fewer forward launches than one song at a time, identical results."""
+    from turbo_roformer_b200 import _lib
+
+    lib = _lib.load()
+    songs = [S.chunk_audio(SR * 2 + 500 * k, seed=80 + k) for k in range(3)]
+    counts = [sep.n_chunks(m.shape[1]) for m in songs]
+    fwd_single = sum(-(-c // sep.batch) for c in counts)
+    fwd_queue = -(-sum(counts) // sep.batch)
+    assert fwd_queue < fwd_single  # the chunk counts are not multiples of the batch
+    n0 = lib.trc_launch_count()
+    ref = [sep.separate(m) for m in songs]
+    n1 = lib.trc_launch_count()
+    jobs = [sep.submit(m) for m in songs]
+    got = [j.result() for j in jobs]
+    n2 = lib.trc_launch_count()
+    for r, g in zip(ref, got):
+        np.testing.assert_array_equal(r, g)
+    per_forward = (n1 - n0 - len(songs)) // fwd_single  # every song also makes one overlap-add launch
+    assert n1 - n0 == fwd_single * per_forward + len(songs)
+    assert n2 - n1 == fwd_queue * per_forward + len(songs)

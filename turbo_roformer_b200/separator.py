@@ -24,7 +24,7 @@ import torch
 
 from . import _lib, audio
 from .backend import CudaBSRoformer
-from .chunking import chunk_starts, overlap_add_cuda, step_for
+from .chunking import chunk_starts, ola_device, overlap_add_cuda, run_chunks, step_for
 from .config import RESURRECTION, infer_config
 
 log = logging.getLogger("turbo_roformer_b200")
@@ -131,7 +131,8 @@ class Separator:
         self.chunk = hop * (dim_t - 1)
         self.backend, self.precision = "cuda", precision
         self.batch = max(1, int(batch))
-        self._lock = threading.Lock()
+        self._lock = threading.RLock()
+        self._pending: list[tuple[SeparationJob, int]] = []  # queued full-length chunks: (job, chunk index)
 
     @classmethod
     def from_module(
@@ -218,14 +219,56 @@ class Separator:
         peak = xd.abs().amax()
         gain = torch.where(peak > PEAK, (PEAK / peak.double()).float(), torch.ones((), device=xd.device))
         xd.mul_(gain)
-        inst = self.separate_device(xd, overlap, progress, check=False)
-        inst.div_(gain)
-        out.copy_(inst[:, :n0], non_blocking=True)
-        flags[1:].copy_((~torch.isfinite(peak)).to(torch.int32).reshape(1), non_blocking=True)
-        self.net.error_async(flags[:1])
-        done = torch.cuda.Event()
-        done.record(torch.cuda.current_stream(self.device))
-        return SeparationJob(self, out, flags, done, keep=(src, xd, inst))
+        n = xd.shape[1]
+        C = min(self.chunk, n)
+        starts = chunk_starts(n, C, step_for(C, overlap))
+        job = SeparationJob(self, out, flags)
+        job._song = _Song(xd, starts, C, n0, gain, peak, torch.empty(len(starts), 2, self.net.output_length(C),
+                                                                    device=xd.device, dtype=torch.float32), src)
+        if C != self.chunk or progress is not None:
+            # a short clip (its own chunk length) or a caller that follows the chunks: its own forwards
+            run_chunks(self.net, xd, starts, C, self.batch, job._song.outs, progress, check=False)
+            job._song.left = 0
+            self._finish(job)
+        else:
+            self._pending.extend((job, i) for i in range(len(starts)))
+            self._run_pending(full_only=True)
+        return job
+
+    def _run_pending(self, full_only: bool) -> None:
+        """Forward the queued chunks ``batch`` at a time, whichever songs they come from (a song's last
+        chunks share a forward with the next song's first ones); the outputs go to each song's chunk
+        buffer and a song whose chunks are all done is overlap-added and copied back. With
+        ``full_only`` a partial batch stays queued for the next song. Forward outputs do not depend on
+        which chunks share a batch, so the result equals one song at a time bit for bit."""
+        while len(self._pending) >= self.batch or (not full_only and self._pending):
+            sel = self._pending[: self.batch]
+            del self._pending[: self.batch]
+            frames = torch.stack([j._song.xd[:, j._song.starts[i] : j._song.starts[i] + j._song.C] for j, i in sel])
+            y = self.net.forward_device(frames, check=False)
+            for k, (j, i) in enumerate(sel):
+                j._song.outs[i].copy_(y[k])
+                j._song.left -= 1
+                if j._song.left == 0:
+                    self._finish(j)
+
+    def _finish(self, job: "SeparationJob") -> None:
+        """Overlap-add, undo the gain, copy the instrumental back and read the error words (queued)."""
+        g = job._song
+        inst = ola_device(g.outs, g.starts, g.C, g.n)
+        inst.div_(g.gain)
+        job._out.copy_(inst[:, : g.n0], non_blocking=True)
+        job._flags[1:].copy_((~torch.isfinite(g.peak)).to(torch.int32).reshape(1), non_blocking=True)
+        self.net.error_async(job._flags[:1])
+        job._done = torch.cuda.Event()
+        job._done.record(torch.cuda.current_stream(self.device))
+        job._keep = (g, inst)
+        job._song = None
+
+    def flush(self) -> None:
+        """Run the chunks still waiting for a full batch (``job.result()`` does this when it needs to)."""
+        with self._lock, torch.inference_mode():
+            self._run_pending(full_only=False)
 
     def _separate_44k(self, x: np.ndarray, overlap: float, progress) -> np.ndarray:
         return self._submit_44k(x, overlap, progress, None).result()
@@ -326,19 +369,38 @@ class Separator:
         )
 
 
-class SeparationJob:
-    """A song queued by ``Separator.submit``. ``result()`` waits for it and returns the instrumental."""
+class _Song:
+    """A queued song's device state until its overlap-add is queued."""
 
-    def __init__(self, sep: Separator, out: torch.Tensor, flags: torch.Tensor, done: torch.cuda.Event, keep):
-        self._sep, self._out, self._flags, self._done, self._keep = sep, out, flags, done, keep
+    def __init__(self, xd, starts, C, n0, gain, peak, outs, src):
+        self.xd, self.starts, self.C, self.n0, self.gain, self.peak, self.outs, self.src = (
+            xd, starts, C, n0, gain, peak, outs, src)
+        self.n = xd.shape[1]
+        self.left = len(starts)
+
+
+class SeparationJob:
+    """A song queued by ``Separator.submit``. ``result()`` waits for it and returns the instrumental.
+
+    Chunks of songs queued back to back share forwards, so a song's last chunks may wait for the next
+    song's (or for ``result()`` / ``Separator.flush()``) to fill a batch."""
+
+    def __init__(self, sep: Separator, out: torch.Tensor, flags: torch.Tensor):
+        self._sep, self._out, self._flags = sep, out, flags
+        self._done: torch.cuda.Event | None = None
+        self._song: _Song | None = None
+        self._keep = None
 
     def done(self) -> bool:
         """True once the GPU has finished the song (non-blocking)."""
-        return self._done.query()
+        return self._done is not None and self._done.query()
 
     def result(self) -> np.ndarray:
         """float32 (2, n) instrumental (a view of the pinned result buffer); raises ValueError on NaN/inf
-        input and TRCError if a kernel reported a device-side error."""
+        input and TRCError if a kernel reported a device-side error (a forward shared with another song
+        reports to the first of the songs that finish after it)."""
+        if self._done is None:
+            self._sep.flush()
         self._done.synchronize()
         self._keep = None
         err, nonfinite = (int(v) for v in self._flags.tolist())
