@@ -91,6 +91,7 @@ def separate_from_host(
     peak_limit: float = 0.9,
     group=None,
     out: torch.Tensor | None = None,
+    post_stream: "torch.cuda.Stream | None" = None,
 ) -> torch.Tensor | None:
     """Sharded separation of one song held in host memory (separator.py:188-201 over the ranks).
 
@@ -100,6 +101,9 @@ def separate_from_host(
     local)`` fills local[i] with the output of the chunk at span[:, s : s + chunk], the outputs are
     gathered to rank 0, which runs the overlap-add, divides by the gain and copies the result into
     ``out`` (if given, asynchronously) or returns it on its device. Other ranks return None.
+
+    ``post_stream`` (CUDA): the gather, overlap-add and copy back run there, after this song's forwards,
+    so rank 0's next song can start computing while this one's result is assembled and copied out.
     """
     rank = dist.get_rank(group)
     world = dist.get_world_size(group)
@@ -121,6 +125,16 @@ def separate_from_host(
     local = torch.zeros(max(counts), 2, out_len, device=device, dtype=torch.float32)
     if hi > lo:
         run_span(span, [s - a for s in starts[lo:hi]], local)
+    if post_stream is None:
+        return _gather_ola(local, counts, starts, chunk, n, gain, ola, group, out, rank)
+    post_stream.wait_stream(torch.cuda.current_stream(device))
+    local.record_stream(post_stream)  # the allocator must not reuse it before the gather has read it
+    gain.record_stream(post_stream)
+    with torch.cuda.stream(post_stream):
+        return _gather_ola(local, counts, starts, chunk, n, gain, ola, group, out, rank)
+
+
+def _gather_ola(local, counts, starts, chunk, n, gain, ola, group, out, rank):
     allc = gather_chunks(local, counts, group)
     if rank != 0:
         return None
@@ -168,7 +182,9 @@ def separate_song_from_host(sep, mix: torch.Tensor, overlap: float = 2.0, out: t
                             group=None) -> torch.Tensor | None:
     """``separate_from_host`` with the ranks' CUDA models: mix (2, n) pinned float32 on the CPU, n >= the
     Separator's chunk; rank 0 gets the (2, n) instrumental (in ``out``, pinned, when given). Work is
-    queued without a host synchronisation; ``sep.net.check()`` reports device-side errors."""
+    queued without a host synchronisation; the gather and overlap-add run on a second stream of the
+    Separator, so synchronise the device (not just the current stream) before reading ``out``;
+    ``sep.net.check()`` reports device-side errors."""
     from .chunking import ola_device, run_chunks
 
     model = sep.net
@@ -177,5 +193,8 @@ def separate_song_from_host(sep, mix: torch.Tensor, overlap: float = 2.0, out: t
     def run_span(span, starts, local):
         run_chunks(model, span, starts, C, sep.batch, local, check=False)
 
+    if getattr(sep, "_post_stream", None) is None:
+        sep._post_stream = torch.cuda.Stream(model.device)
     return separate_from_host(mix, C, overlap, run_span, model.output_length(C), model.device,
-                              lambda ch, st, c, n: ola_device(ch, st, c, n), group=group, out=out)
+                              lambda ch, st, c, n: ola_device(ch, st, c, n), group=group, out=out,
+                              post_stream=sep._post_stream)
