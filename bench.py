@@ -308,7 +308,7 @@ def event_times(fn, runs: int, warmup: int = 3) -> list[float]:
     return out
 
 
-def extras(sep, cfg, sd, pk) -> dict:
+def extras(sep, cfg, sd, pk, precision: str = "fp16") -> dict:
     """Config 1 latency at batch 1, config 2 (isolated time attention) and config 3 (stack alone)."""
     from oracle import roformer_oracle as R
     from turbo_roformer_b200 import _lib
@@ -334,9 +334,10 @@ def extras(sep, cfg, sd, pk) -> dict:
     freqs = S.rotary_freqs(64)
     q = R.rotate(q, freqs) * 0.125
     k = R.rotate(k, freqs)
-    qd, kd, vd = (t.to(dev, torch.float16).contiguous() for t in (q, k, v))
+    op_dtype = torch.float16 if precision == "fp16" else torch.bfloat16
+    qd, kd, vd = (t.to(dev, op_dtype).contiguous() for t in (q, k, v))
     G = torch.ones(T1 * F, 8, device=dev)
-    O = torch.empty(T1 * F, 512, device=dev, dtype=torch.float16)
+    O = torch.empty(T1 * F, 512, device=dev, dtype=op_dtype)
     st = ctypes.c_void_p(m.stream_ptr())
     ptr = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
 
@@ -348,7 +349,7 @@ def extras(sep, cfg, sd, pk) -> dict:
     fl = 4.0 * T1 * T1 * 64 * F * 8
     med = float(np.median(ts))
     res["config2_time_attention"] = {
-        "shape": [F * 8, T1, 64], "dtype": "f16", "median_ms": med, "tflops": fl / (med / 1e3) / 1e12,
+        "shape": [F * 8, T1, 64], "dtype": "f16" if precision == "fp16" else "bf16", "median_ms": med, "tflops": fl / (med / 1e3) / 1e12,
         "frac": fl / (med / 1e3) / 1e12 / pk["tc_sustained"], "runs": len(ts)}
     # config 3: the 24 transformers alone on tokens [1701 * 62, 256] ~ N(0,1) (bf16-representable)
     X0 = torch.randn(T1 * F, 256, generator=g).to(torch.bfloat16).float().to(dev)
@@ -389,6 +390,7 @@ def main() -> None:
     ap.add_argument("--batch", type=int, default=8, help="chunks per forward call (8: 8+8+8+5 for the song)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="skip the config 1/2/3 timings at N=1")
+    ap.add_argument("--precision", default="fp16", choices=("fp16", "bf16"), help="tensor-core operand type")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
@@ -428,7 +430,7 @@ def main() -> None:
 
     cfg = C.RESURRECTION
     sd = S.init_weights(cfg, seed=0)
-    sep = Separator.from_state_dict(sd, hop=cfg.stft_hop_length, dim_t=cfg.dim_t, precision="fp16", device=local,
+    sep = Separator.from_state_dict(sd, hop=cfg.stft_hop_length, dim_t=cfg.dim_t, precision=args.precision, device=local,
                                     batch=args.batch)
     lib = _lib.load()
     chunk = sep.chunk
@@ -521,6 +523,7 @@ def main() -> None:
     #     copies the outputs back.
     barrier()
     torch.cuda.synchronize()
+    e2e_clk = None
     if args.workload == "song":
         pinned = torch.from_numpy(song).pin_memory()
         if world == 1:
@@ -530,10 +533,12 @@ def main() -> None:
             for j in [sep.submit(pinned, overlap=OVERLAP, out=outs[k]) for k in range(args.steps)]:
                 j.result()
             torch.cuda.synchronize()
+            e2e_clocks = ClockSampler(local)
             t0 = time.perf_counter()
             jobs = [sep.submit(pinned, overlap=OVERLAP, out=outs[k]) for k in range(args.steps)]
             results = [j.result() for j in jobs]
             ms_e2e = 1e3 * (time.perf_counter() - t0)
+            e2e_clk = e2e_clocks.stop()
             assert all(r.shape == song.shape for r in results)
             h2d = song.nbytes
         else:
@@ -600,15 +605,17 @@ def main() -> None:
     line = {
         "metric": metric, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms / args.steps, "step_ms": step_ms, "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": value / PUBLISHED if args.workload == "song" else None, "dtype": "f16", "data": "synthetic",
+        "vs_baseline": value / PUBLISHED if args.workload == "song" else None,
+        "dtype": "f16" if args.precision == "fp16" else "bf16", "data": "synthetic",
         "config": config,
         "ms_per_chunk_amortised": (ms / args.steps) / n_chunks * world,
-        "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                **({"clocks": e2e_clk} if e2e_clk else {})},
         "gpu_launches": launches, "clocks": clk, "roofline": roofline,
         "sections_ms": {k: round(v[0], 3) for k, v in sorted(sections.items())},
     }
     if rank == 0 and world == 1 and not args.no_extras:
-        line.update(extras(sep, cfg, sd, pk))
+        line.update(extras(sep, cfg, sd, pk, args.precision))
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = host_cpu()
         tune_host_malloc()

@@ -188,8 +188,8 @@ int trc_stft(trc_handle* h, const float* d_audio, int batch, int64_t samples, fl
 int trc_band_split(trc_handle* h, const float* d_xin, int batch, int T, float* d_X, void* stream);
 
 /* fast.py:385-387 + 349-360: xn (L2-normalised last residual, [tokens][256] 16-bit) -> mask
- * [batch][T][n_fft/2+1][2][2] fp32 (final norm gain folded into the first mask layer). d_hidden is
- * scratch of n_bands * batch * T * dim * mlp_expansion_factor 16-bit elements. */
+ * [batch][T][n_fft/2+1][2][2] fp32 (final norm gain folded into the first mask layer; d_mask 16-byte
+ * aligned). d_hidden is scratch of n_bands * batch * T * dim * mlp_expansion_factor 16-bit elements. */
 int trc_mask(trc_handle* h, const void* d_xn, int batch, int T, float* d_mask, void* d_hidden, void* stream);
 
 /* fast.py:388-393: mask apply + iSTFT. xin, mask as above -> out [batch][2][hop * (T - 1)].

@@ -661,7 +661,17 @@ int run_band_split(trc_handle* h, const float* xin, int B, int T, float* X, void
   if ((rc = check_launch(cudaGetLastError(), "band pack"))) return rc;
   CUtensorMap ma;
   if ((rc = map_2d_cached(h, &ma, h->bs_a.p, h->bs_kp, rows, 128))) return rc;
-  const CUtensorMap mo[3] = {ma, ma, ma};  // the epilogue stores directly
+  // X (fp32) and xn (16-bit) as 3-D views (256, bands, rows), stored by TMA in boxes of 32 rows of one
+  // band: 32 columns of X, 64 of xn
+  CUtensorMap mo[3];
+  {
+    const uint64_t dims[3] = {256, (uint64_t)nb, (uint64_t)rows};
+    const uint64_t st_x[2] = {256 * 4, (uint64_t)nb * 256 * 4}, st_n[2] = {256 * 2, (uint64_t)nb * 256 * 2};
+    const uint32_t box_x[3] = {32, 1, 32}, box_n[3] = {64, 1, 32};
+    if ((rc = make_map_cached(h, &mo[0], X, 3, dims, st_x, box_x, kMapF32))) return rc;
+    if ((rc = make_map_cached(h, &mo[1], xn, 3, dims, st_n, box_n))) return rc;
+    mo[2] = mo[1];
+  }
   GemmArgs a;
   std::memset(&a, 0, sizeof(a));
   a.a_mode = trc::A_BAND;
@@ -1212,7 +1222,8 @@ int trc_band_split(trc_handle* h, const float* d_xin, int batch, int T, float* d
 
 int trc_mask(trc_handle* h, const void* d_xn, int batch, int T, float* d_mask, void* d_hidden, void* stream) {
   TRC_REQUIRE_PREPARED(h);
-  if (batch < 1 || T < 1 || !d_hidden) return fail(TRC_E_INVALID, "bad mask arguments");
+  if (batch < 1 || T < 1 || !d_hidden || !d_xn || !d_mask) return fail(TRC_E_INVALID, "bad mask arguments");
+  if (reinterpret_cast<uintptr_t>(d_mask) % 16) return fail(TRC_E_INVALID, "mask must be 16-byte aligned");
   Section sec(h, "mask", (cudaStream_t)stream, 2);
   return run_mask(h, d_xn, batch, T, d_mask, d_hidden, (cudaStream_t)stream);
 }

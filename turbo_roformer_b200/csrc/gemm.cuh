@@ -556,67 +556,101 @@ __device__ __forceinline__ void epi_glu(const GemmArgs& a, const TileCoord& tc, 
     tmem_ld32(e.taddr + col, v);
     if (valid) {
       const int col0 = tc.n0 + col;  // interleaved column: (a, g) pairs
+      float r[16];
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
-        const int cc = (col0 >> 1) + i;
-        if (cc < din) {
-          const float av = v[2 * i] + bias[col + 2 * i];
-          const float gv = v[2 * i + 1] + bias[col + 2 * i + 1];
-          out[cc] = av * sigmoidf_(gv);
-        }
+        const float av = v[2 * i] + bias[col + 2 * i];
+        const float gv = v[2 * i + 1] + bias[col + 2 * i + 1];
+        r[i] = av * sigmoidf_(gv);
+      }
+      const int c0 = col0 >> 1;  // a multiple of 16: 16-byte aligned in the row (the row stride is too)
+      if (c0 + 16 <= din) {
+        float4* o4 = reinterpret_cast<float4*>(out + c0);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) o4[q] = make_float4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          if (c0 + i < din) out[c0 + i] = r[i];
       }
     }
   }
 }
 
-// Band split + first norm (EPI_BAND): each thread owns one row (frame) and one column half of the
-// band's 256 outputs. X = acc + b is written as fp32 (512 contiguous bytes per thread), the two halves
-// of a row meet in shared memory with their sums of squares, and xn = X / max(|X|, eps) is written as
-// 16-bit from a second read of the accumulator. X [rows][bands][256] fp32 (out0), xn the same in 16 bits
-// (out1). Returns false if the row-sum exchange was abandoned (a failed wait elsewhere).
+// Band split + first norm (EPI_BAND): each epilogue warp owns 32 rows (frames) x 128 columns (its half)
+// of one band's 256 outputs and two 4 KB shared-memory boxes (128-byte swizzle), stored by TMA into the
+// 3-D views X (256, bands, rows) fp32 and xn (256, bands, rows) 16-bit, so every global write is a whole
+// line. Pass 1: X = acc + b, 32 columns per box, and the row's sum of squares; the two column halves meet
+// in shared memory; pass 2: xn = X / max(|X|, eps) from a second read of the accumulator, 64 columns
+// per box. Returns false if the row-sum exchange was abandoned (a failed wait elsewhere).
 template <int BN, typename TIn>
-__device__ __forceinline__ bool epi_band(const GemmArgs& a, const TileCoord& tc, EpiCtx& e, float* rs_base,
+__device__ __forceinline__ bool epi_band(const GemmArgs& a, const TileCoord& tc, EpiCtx& e, uint8_t* box,
+                                         const CUtensorMap* map_x, const CUtensorMap* map_xn, float* rs_base,
                                          int local_tile) {
   static_assert(BN == 256, "the band epilogue covers whole 256-wide rows");
-  const int m = tc.m0 + e.row;
-  const bool valid = m < a.M;
-  const size_t row_off = ((size_t)m * a.F + tc.group) * 256 + e.hf * 128;
+  const int lane = e.lane;
+  const int row0 = tc.m0 + e.quarter * 32;
+  const bool live = row0 < a.M;  // a warp whose 32 rows all lie past M stores nothing
+  const int swz = lane & 7;
   const float* bias = a.bias + tc.group * 256 + e.hf * 128;
+  if (lane == 0) bulk_wait_read<0>();  // the previous tile's stores have read both boxes
+  __syncwarp();
   float ss = 0.f;
 #pragma unroll 1
   for (int c = 0; c < 4; ++c) {
+    uint8_t* rowp = box + (c & 1) * kResBoxBytes + lane * 128;
+    if (c >= 2) {  // the store from this box two chunks ago has read it
+      if (lane == 0) bulk_wait_read<1>();
+      __syncwarp();
+    }
     float v[32];
     tmem_ld32(e.taddr + e.hf * 128 + c * 32, v);
     const float4* b4 = reinterpret_cast<const float4*>(bias + c * 32);
-    float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out0) + row_off + c * 32);
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
       const float4 b = __ldg(b4 + q);
       const float4 x = make_float4(v[4 * q] + b.x, v[4 * q + 1] + b.y, v[4 * q + 2] + b.z, v[4 * q + 3] + b.w);
       ss = fmaf(x.x, x.x, fmaf(x.y, x.y, fmaf(x.z, x.z, fmaf(x.w, x.w, ss))));
-      if (valid) dst[q] = x;
+      *reinterpret_cast<float4*>(rowp + ((q ^ swz) << 4)) = x;
+    }
+    fence_async_smem();
+    __syncwarp();
+    if (lane == 0 && live) {
+      tma_store_3d(map_x, box + (c & 1) * kResBoxBytes, e.hf * 128 + c * 32, tc.group, row0);
+      bulk_commit();
     }
   }
   float* rs = rs_base + (local_tile & 1) * 256;
-  rs[e.hf * 128 + e.quarter * 32 + e.lane] = ss;
+  rs[e.hf * 128 + e.quarter * 32 + lane] = ss;
   if (!named_bar_and(3, 32 * kEpiWarps, true)) return false;
-  const float tot = rs[e.quarter * 32 + e.lane] + rs[128 + e.quarter * 32 + e.lane];
+  const float tot = rs[e.quarter * 32 + lane] + rs[128 + e.quarter * 32 + lane];
   const float inv = 1.0f / fmaxf(sqrtf(tot), a.eps);
+  if (lane == 0) bulk_wait_read<0>();  // both boxes free for the 16-bit output
+  __syncwarp();
 #pragma unroll 1
-  for (int c = 0; c < 4; ++c) {
-    float v[32];
-    tmem_ld32(e.taddr + e.hf * 128 + c * 32, v);
-    const float4* b4 = reinterpret_cast<const float4*>(bias + c * 32);
-    uint4* dst = reinterpret_cast<uint4*>(static_cast<TIn*>(a.out1) + row_off + c * 32);
+  for (int k = 0; k < 2; ++k) {
+    uint8_t* rowp = box + k * kResBoxBytes + lane * 128;
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const float4 b0 = __ldg(b4 + 2 * q), b1 = __ldg(b4 + 2 * q + 1);
-      uint4 u;
-      u.x = OperandType<TIn>::pack2((v[8 * q] + b0.x) * inv, (v[8 * q + 1] + b0.y) * inv);
-      u.y = OperandType<TIn>::pack2((v[8 * q + 2] + b0.z) * inv, (v[8 * q + 3] + b0.w) * inv);
-      u.z = OperandType<TIn>::pack2((v[8 * q + 4] + b1.x) * inv, (v[8 * q + 5] + b1.y) * inv);
-      u.w = OperandType<TIn>::pack2((v[8 * q + 6] + b1.z) * inv, (v[8 * q + 7] + b1.w) * inv);
-      if (valid) dst[q] = u;
+    for (int h = 0; h < 2; ++h) {
+      float v[32];
+      tmem_ld32(e.taddr + e.hf * 128 + (2 * k + h) * 32, v);
+      const float4* b4 = reinterpret_cast<const float4*>(bias + (2 * k + h) * 32);
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const float4 b0 = __ldg(b4 + 2 * t), b1 = __ldg(b4 + 2 * t + 1);
+        uint4 u;
+        u.x = OperandType<TIn>::pack2((v[8 * t] + b0.x) * inv, (v[8 * t + 1] + b0.y) * inv);
+        u.y = OperandType<TIn>::pack2((v[8 * t + 2] + b0.z) * inv, (v[8 * t + 3] + b0.w) * inv);
+        u.z = OperandType<TIn>::pack2((v[8 * t + 4] + b1.x) * inv, (v[8 * t + 5] + b1.y) * inv);
+        u.w = OperandType<TIn>::pack2((v[8 * t + 6] + b1.z) * inv, (v[8 * t + 7] + b1.w) * inv);
+        *reinterpret_cast<uint4*>(rowp + (((h * 4 + t) ^ swz) << 4)) = u;
+      }
+    }
+    fence_async_smem();
+    __syncwarp();
+    if (lane == 0 && live) {
+      tma_store_3d(map_xn, box + k * kResBoxBytes, e.hf * 128 + k * 64, tc.group, row0);
+      bulk_commit();
     }
   }
   return true;
@@ -889,7 +923,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       } else if constexpr (EPI == EPI_MASK_TANH) {
         epi_act<BN, TIn>(args, tc, e, &map_o0, true);
       } else if constexpr (EPI == EPI_BAND) {
-        if (!epi_band<BN, TIn>(args, tc, e, reinterpret_cast<float*>(smem + S::kRsOffset), local)) {
+        if (!epi_band<BN, TIn>(args, tc, e, rst.box, &map_o0, &map_o1, reinterpret_cast<float*>(smem + S::kRsOffset),
+                               local)) {
           run = false;
           break;
         }
@@ -900,8 +935,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_arrive(&acc_empty[buf]);
     }
     }
-    if constexpr (EPI == EPI_RESNORM) {
-      resnorm_drain(e, rst);
+    if constexpr (EPI == EPI_RESNORM || EPI == EPI_BAND) {
+      if constexpr (EPI == EPI_RESNORM) resnorm_drain(e, rst);
       if (lane == 0) bulk_wait<0>();  // this warp's stores have completed
     } else {
       if (e.leader) bulk_wait<0>();  // this half's output stores have completed
