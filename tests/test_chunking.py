@@ -78,3 +78,31 @@ def test_progress_callback_counts():
 def test_invalid_schedule_arguments():
     with pytest.raises(ValueError):
         chunk_starts(0, 10, 5)
+
+
+def test_stream_plan_reproduces_the_schedule():
+    """Streaming the schedule over random arrival patterns runs exactly chunk_starts(n) in start order, and
+    every chunk of the final schedule that covers a sample reported final has already run."""
+    import random
+
+    from turbo_roformer_b200.chunking import chunk_starts, stream_plan
+
+    rnd = random.Random(1)
+    for _ in range(5000):
+        C = rnd.randint(1, 50)
+        step = rnd.randint(1, C)
+        n_final = rnd.randint(C, 400)
+        cuts = sorted(rnd.sample(range(1, n_final), min(n_final - 1, rnd.randint(0, 10)))) + [n_final]
+        full = chunk_starts(n_final, C, step)
+        nxt, ran, final_end = 0, [], 0
+        for n in cuts:
+            st, end = stream_plan(n, nxt, C, step, final=False)
+            ran += st
+            if st:
+                nxt = st[-1] + step
+            assert end >= final_end
+            final_end = end
+            assert all(s in ran for s in full if s < end)
+        st, end = stream_plan(n_final, nxt, C, step, final=True)
+        ran += st
+        assert ran == full and end == n_final

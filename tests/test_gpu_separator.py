@@ -184,3 +184,67 @@ def test_queued_songs_share_forwards(sep):
     per_forward = (n1 - n0 - len(songs)) // fwd_single  # every song also makes one overlap-add launch
     assert n1 - n0 == fwd_single * per_forward + len(songs)
     assert n2 - n1 == fwd_queue * per_forward + len(songs)
+
+
+def _stream_all(sep, mix, blocks, gain=1.0, overlap=2.0):
+    st = sep.stream(overlap=overlap, gain=gain)
+    parts, i = [], 0
+    for b in blocks:
+        out = st.push(mix[:, i : i + b])
+        i += b
+        assert out.dtype == np.float32 and out.shape[0] == 2
+        assert st.samples_out == sum(p.shape[1] for p in parts) + out.shape[1]
+        assert st.samples_out <= max(0, i - sep.chunk) or st.samples_out == 0
+        parts.append(out)
+    assert i == mix.shape[1]
+    parts.append(st.close())
+    return np.concatenate(parts, axis=1)
+
+
+@pytest.mark.parametrize("overlap", [2.0, 3.0])
+def test_stream_equals_separate(sep, overlap):
+    """Blocks of every size (empty, a few samples, more than a chunk): the concatenated stream output
+    equals separate() bit for bit; output lags the input by one chunk."""
+    C = sep.chunk
+    mix = S.chunk_audio(3 * C + 1234, seed=21)
+    mix *= np.float32(0.5 / np.abs(mix).max())  # peak 0.5: separate() applies no gain
+    rng = np.random.default_rng(3)
+    blocks, left = [], mix.shape[1]
+    while left:
+        b = int(min(left, rng.choice([0, 1, 7, 441, C // 3, C, C + 5])))
+        blocks.append(b)
+        left -= b
+    got = _stream_all(sep, mix, blocks, overlap=overlap)
+    np.testing.assert_array_equal(got, sep.separate(mix, overlap=overlap))
+
+
+def test_stream_with_separate_gain(sep):
+    """A loud mix: with the float32 gain separate() computes (0.9 / peak), the stream matches it."""
+    C = sep.chunk
+    mix = S.chunk_audio(2 * C + 77, seed=22) * np.float32(2.0)
+    gain = float(np.float32(0.9 / np.float64(np.abs(mix).max())))
+    got = _stream_all(sep, mix, [C // 2] * 4 + [mix.shape[1] - 4 * (C // 2)], gain=gain)
+    np.testing.assert_array_equal(got, sep.separate(mix))
+
+
+@pytest.mark.parametrize("extra", [-300, 0, 1])
+def test_stream_short_and_one_chunk(sep, extra):
+    """Shorter than a chunk (the short-clip path at close), exactly one chunk, one sample more."""
+    n = sep.chunk + extra
+    mix = S.chunk_audio(n, seed=23) * np.float32(0.4)
+    got = _stream_all(sep, mix, [n // 3, n - n // 3])
+    np.testing.assert_array_equal(got, sep.separate(mix))
+
+
+def test_stream_errors(sep):
+    st = sep.stream()
+    with pytest.raises(ValueError):
+        st.push(np.full((2, 10), np.nan, np.float32))
+    with pytest.raises(ValueError):
+        st.push(np.zeros((3, 10), np.float32))
+    with pytest.raises(ValueError):
+        st.close()  # nothing pushed
+    with pytest.raises(RuntimeError):
+        st.push(np.zeros((2, 10), np.float32))
+    with pytest.raises(ValueError):
+        sep.stream(gain=0.0)

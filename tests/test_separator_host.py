@@ -116,3 +116,59 @@ def test_cuda_backend_fails_loudly_without_gpu(tiny_sd):
 
     with pytest.raises(KernelUnavailable):
         Separator.from_module(tiny_sd, 128, 128)
+
+
+class _FakeNet:
+    """A batch-invariant stand-in for the CUDA model on the CPU: y = tanh(3 x) over whole hops."""
+
+    hop = 7
+
+    def output_length(self, n):
+        return self.hop * (n // self.hop)
+
+    def forward_device(self, frames, out=None, check=True):
+        y = torch.tanh(frames[..., : self.output_length(frames.shape[-1])] * 3.0)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
+
+    def check(self):
+        pass
+
+
+def _fake_separator(monkeypatch, chunk, batch):
+    import threading
+
+    monkeypatch.setattr(Separator, "device", property(lambda self: torch.device("cpu")))
+    sep = Separator.__new__(Separator)
+    sep.net, sep.chunk, sep.hop, sep.batch = _FakeNet(), chunk, _FakeNet.hop, batch
+    sep._lock = threading.RLock()
+    sep._pending = []
+    return sep
+
+
+@pytest.mark.parametrize("overlap,batch", [(2.0, 1), (3.0, 3), (1.5, 2)])
+def test_stream_logic_matches_whole_song_overlap_add(monkeypatch, overlap, batch):
+    """Separator.stream on a CPU stand-in model (the device overlap-add replaced by the oracle's loop):
+    the concatenated blocks equal the whole-song overlap-add of the same model bit for bit."""
+    from turbo_roformer_b200 import separator as SP
+
+    monkeypatch.setattr(SP, "ola_device", lambda ys, starts, C, n: O.ola_from_outputs(list(ys), starts, n, C))
+    monkeypatch.setattr(SP, "overlap_add_cuda", lambda net, x, chunk, ov, batch: O.overlap_add(x, chunk, ov, net.forward_device))
+    C = 7 * 40
+    sep = _fake_separator(monkeypatch, C, batch)
+    rng = np.random.default_rng(5)
+    for n in (5, 30, C - 3, C, C + 1, 3 * C + 17, 5 * C):
+        mix = rng.standard_normal((2, n)).astype(np.float32)
+        mix *= np.float32(0.5 / np.abs(mix).max())
+        ref = O.separate_44k(mix, C, _FakeNet.hop, overlap, sep.net.forward_device)
+        st = sep.stream(overlap=overlap)
+        parts, i = [], 0
+        while i < n:
+            b = int(rng.choice([0, 1, 5, 33, C // 2, C + 3]))
+            parts.append(st.push(mix[:, i : i + b]))
+            i += b
+            assert st.samples_out == max(0, min(i, n) - C)
+        parts.append(st.close())
+        np.testing.assert_array_equal(np.concatenate(parts, axis=1), ref)

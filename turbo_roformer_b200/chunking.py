@@ -49,6 +49,27 @@ def hamming(n: int) -> np.ndarray:
     return (0.54 - 0.46 * np.cos(2.0 * np.pi * k / (n - 1))).astype(np.float32)
 
 
+def stream_plan(n: int, next_start: int, chunk: int, step: int, final: bool) -> tuple[list[int], int]:
+    """One step of streaming the schedule of ``chunk_starts`` while the length is still growing.
+
+    ``n`` samples have arrived, the regular chunks before ``next_start`` have run. Returns the starts to
+    run now and the end of the samples that are final after them. A regular start s is certain once
+    s + chunk < n (the total only grows); the tail chunk ends at the total length, so it starts at or after
+    n - chunk, and every sample before n - chunk has all of its chunks among the regular ones. With
+    ``final`` the length is n: the rest of ``chunk_starts(n, chunk, step)`` runs and everything is final;
+    the tail chunk may start before ``next_start`` (it starts after every regular chunk that ran, since
+    those end before n). (Requires n >= chunk when ``final``: a shorter clip takes the separator's
+    short-clip path.)"""
+    if final:
+        return [s for s in chunk_starts(n, chunk, step) if not (s < next_start and s % step == 0)], n
+    starts = []
+    s = next_start
+    while s + chunk < n:
+        starts.append(s)
+        s += step
+    return starts, max(0, n - chunk)
+
+
 def overlap_add(
     x: torch.Tensor,
     chunk: int,

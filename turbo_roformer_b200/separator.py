@@ -24,7 +24,7 @@ import torch
 
 from . import _lib, audio
 from .backend import CudaBSRoformer
-from .chunking import chunk_starts, ola_device, overlap_add_cuda, run_chunks, step_for
+from .chunking import chunk_starts, ola_device, overlap_add_cuda, run_chunks, step_for, stream_plan
 from .config import RESURRECTION, infer_config
 
 log = logging.getLogger("turbo_roformer_b200")
@@ -172,13 +172,15 @@ class Separator:
         C = min(self.chunk, n_samples)
         return len(chunk_starts(n_samples, C, step_for(C, overlap)))
 
-    def _pad_short(self, x: np.ndarray) -> np.ndarray:
+    def _padded_length(self, n0: int) -> int:
         """Clips shorter than one chunk are zero-padded to whole hops, at least 3 (separator.py:190-193)."""
-        n0 = x.shape[1]
         if n0 < self.chunk and (n0 % self.hop or n0 < 3 * self.hop):
-            target = max(-(-n0 // self.hop) * self.hop, 3 * self.hop)
-            x = np.pad(x, ((0, 0), (0, target - n0)))
-        return x
+            return max(-(-n0 // self.hop) * self.hop, 3 * self.hop)
+        return n0
+
+    def _pad_short(self, x: np.ndarray) -> np.ndarray:
+        target = self._padded_length(x.shape[1])
+        return np.pad(x, ((0, 0), (0, target - x.shape[1]))) if target != x.shape[1] else x
 
     def prepare_44k(self, x: np.ndarray) -> tuple[np.ndarray, float]:
         """Short-clip padding and peak gain (separator.py:190-197): returns (padded x * gain, gain)."""
@@ -295,6 +297,20 @@ class Separator:
         with self._lock:
             return self._submit_44k(x, float(overlap), None, out)
 
+    def stream(self, overlap: float = 2.0, gain: float = 1.0) -> "SeparationStream":
+        """Separate a 44.1 kHz stereo stream as it arrives: ``push`` blocks, ``close`` at the end.
+
+        The streaming API of the reference's roadmap (README.md:139). The chunk schedule, overlap-add and
+        forward are ``separate``'s, so the blocks the stream returns, concatenated, equal
+        ``separate(whole_mix)`` bit for bit whenever ``gain`` is the gain ``separate`` applies (1.0 for a
+        mix whose peak is at most 0.9; else the float32 value of 0.9 / peak). A stream cannot see the
+        peak ahead of time, so the caller chooses the gain. Output lags the input by one chunk."""
+        if not overlap >= 1.0:
+            raise ValueError("overlap must be >= 1")
+        if not (np.isfinite(gain) and gain > 0):
+            raise ValueError("gain must be a positive finite number")
+        return SeparationStream(self, float(overlap), float(gain))
+
     def separate(
         self,
         mix,
@@ -409,3 +425,115 @@ class SeparationJob:
         if nonfinite:
             raise ValueError("input contains NaN or inf samples")
         return self._out.numpy()
+
+
+class SeparationStream:
+    """Incremental separation (``Separator.stream``): ``push(block)`` returns the instrumental samples that
+    became final, ``close()`` the rest.
+
+    Regular chunks run as soon as all of their samples and one more have arrived (their start s has
+    s + chunk < samples so far, so they belong to the final schedule); a sample is final once it lies
+    before the last chunk length of the input, which the tail chunk (aligned to the end) cannot reach.
+    Each returned segment is the device overlap-add of every chunk that covers it, in start order, so its
+    values are those of the whole-song overlap-add. Only the samples later chunks still read and the
+    outputs of chunks that reach past the returned samples stay on the GPU."""
+
+    def __init__(self, sep: Separator, overlap: float, gain: float):
+        self._sep = sep
+        self._C = sep.chunk
+        self._overlap = overlap
+        self._step = step_for(self._C, overlap)
+        self._gain = torch.tensor(gain, dtype=torch.float32, device=sep.device)
+        self._x = torch.empty(2, 0, device=sep.device, dtype=torch.float32)  # samples [_base, _n), gain applied
+        self._base = 0
+        self._n = 0
+        self._next = 0                     # next regular chunk start
+        self._starts: list[int] = []       # chunks whose outputs are still needed, in start order
+        self._outs: list[torch.Tensor] = []
+        self._emitted = 0
+        self._closed = False
+
+    @property
+    def samples_in(self) -> int:
+        return self._n
+
+    @property
+    def samples_out(self) -> int:
+        return self._emitted
+
+    def _block(self, block) -> torch.Tensor:
+        a = block.numpy() if isinstance(block, torch.Tensor) else np.asarray(block)
+        if a.dtype.kind != "f":
+            raise ValueError(f"expected floating point samples, got dtype {a.dtype}")
+        if a.ndim == 1:
+            a = np.stack([a, a])
+        if a.ndim != 2 or a.shape[0] != 2:
+            raise ValueError(f"expected a (2, samples) or (samples,) block, got shape {a.shape}")
+        audio.check_finite(a)
+        return torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32))
+
+    def push(self, block) -> np.ndarray:
+        """Append a (2, k) float32 block (or mono (k,)); returns the (2, m) instrumental samples now final."""
+        if self._closed:
+            raise RuntimeError("stream is closed")
+        xb = self._block(block)
+        if xb.shape[1] == 0:
+            return np.zeros((2, 0), np.float32)
+        with self._sep._lock, torch.inference_mode():
+            xd = xb.to(self._sep.device).mul_(self._gain)
+            self._x = torch.cat([self._x, xd], dim=1)
+            self._n += xd.shape[1]
+            starts, end = stream_plan(self._n, self._next, self._C, self._step, final=False)
+            if starts:
+                self._next = starts[-1] + self._step
+            return self._advance(starts, end)
+
+    def close(self) -> np.ndarray:
+        """End of input: run the remaining chunks and return the rest of the instrumental."""
+        if self._closed:
+            raise RuntimeError("stream is closed")
+        self._closed = True
+        if self._n == 0:
+            raise ValueError("empty input")
+        with self._sep._lock, torch.inference_mode():
+            if self._n < self._C:  # a clip shorter than one chunk: the separator's short-clip path
+                sep = self._sep
+                xd = torch.nn.functional.pad(self._x, (0, sep._padded_length(self._n) - self._n))
+                inst = overlap_add_cuda(sep.net, xd, sep.chunk, self._overlap, batch=sep.batch)
+                inst.div_(self._gain)
+                self._emitted = self._n
+                return inst[:, : self._n].cpu().numpy()
+            starts, end = stream_plan(self._n, self._next, self._C, self._step, final=True)
+            return self._advance(starts, end)
+
+    def _advance(self, starts: list[int], end: int) -> np.ndarray:
+        sep, C = self._sep, self._C
+        for b0 in range(0, len(starts), sep.batch):
+            sel = starts[b0 : b0 + sep.batch]
+            frames = torch.stack([self._x[:, s - self._base : s - self._base + C] for s in sel])
+            y = sep.net.forward_device(frames, check=False)
+            self._starts += sel
+            self._outs += list(y)
+        if end <= self._emitted:
+            sep.net.check()
+            return np.zeros((2, 0), np.float32)
+        # the chunks that cover [_emitted, end): all kept chunks from the first one reaching past _emitted
+        L = sep.net.output_length(C)
+        first = next(i for i, s in enumerate(self._starts) if s + L > self._emitted)
+        last = max(i for i, s in enumerate(self._starts) if s < end)
+        s0 = self._starts[first]
+        rel = [s - s0 for s in self._starts[first : last + 1]]
+        ola = ola_device(torch.stack(self._outs[first : last + 1]), rel, C, rel[-1] + C)
+        seg = ola[:, self._emitted - s0 : end - s0].div_(self._gain).cpu().numpy()
+        sep.net.check()
+        self._emitted = end
+        # drop what later segments no longer read: chunk outputs that end at or before `end`, and the
+        # input before the earliest start a later chunk can have (the next regular start or the tail's)
+        keep = [i for i, s in enumerate(self._starts) if s + L > end]
+        self._starts = [self._starts[i] for i in keep]
+        self._outs = [self._outs[i] for i in keep]
+        cut = min(self._next, max(0, self._n - C)) - self._base
+        if cut > 0:
+            self._x = self._x[:, cut:].contiguous()
+            self._base += cut
+        return seg
