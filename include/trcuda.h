@@ -105,6 +105,20 @@ int trc_ola(const float* d_chunks, int64_t chunk_out_len, const int64_t* h_start
 
 const char* trc_last_error(void);
 
+/* Replaces audio.to_stereo / downmix_stereo (turbo_roformer/audio.py:35-68) on the device:
+ * d_out[o][i] = (float)(sum over k of h_gains[o * channels + k] * (double)d_in[k][i]), k ascending, fp64.
+ * d_in [channels][n] float32; h_gains: host (2 x channels) float64 row-major, copied into the launch;
+ * 1 <= channels <= 16; d_out [2][n]. */
+int trc_remix(const float* d_in, int channels, int64_t n, const double* h_gains, float* d_out, void* stream);
+
+/* Replaces audio.resample (turbo_roformer/audio.py:71-82, soxr there) on the device: polyphase FIR
+ * resampling by up/down of each of `channels` rows. Output m: t = m * down + half, j0 = t / up,
+ * p = t % up, d_out[c][m] = (float)(sum over k < k_per_phase of d_taps[k * up + p] * (double)d_in[c][j0 - k]),
+ * inputs outside [0, n_in) being zero. d_taps [k_per_phase][up] float64 on the device: the caller's
+ * filter h (odd length 2 * half + 1, gain `up` included) with d_taps[k * up + p] = h[p + k * up]. */
+int trc_resample(const float* d_in, int channels, int64_t n_in, int up, int down, int64_t half, const double* d_taps,
+                 int k_per_phase, int64_t n_out, float* d_out, void* stream);
+
 /* Overlap-add that allocates nothing. No counterpart in the reference: it exists for callers that may
  * not allocate device memory while they run (an audio plugin whose host application owns all device
  * memory and forbids allocations of its own, a real-time audio thread that must not block in the

@@ -70,6 +70,8 @@ SIGNATURES = {
     "trc_selftest_wait_timeout": (c_int, [c_vp, c_vp]),
     "trc_ola": (c_int, [c_vp, c_i64, c_vp, c_int, c_i64, c_i64, c_vp, c_vp]),
     "trc_last_error": (c_char_p, []),
+    "trc_remix": (c_int, [c_vp, c_int, c_i64, c_vp, c_vp, c_vp]),
+    "trc_resample": (c_int, [c_vp, c_int, c_i64, c_int, c_int, c_i64, c_vp, c_int, c_i64, c_vp, c_vp]),
     "trc_ola_noalloc": (c_int, [c_vp, c_i64, c_vp, c_int, c_i64, c_i64, c_vp, c_vp]),
     "trc_profile": (c_int, [c_vp, c_int]),
     "trc_profile_read": (c_int, [c_vp, c_char_p, c_int]),

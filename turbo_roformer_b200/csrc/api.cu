@@ -1123,6 +1123,25 @@ int trc_ola(const float* d_chunks, int64_t chunk_out_len, const int64_t* h_start
   return check_launch(e, "overlap-add");
 }
 
+int trc_remix(const float* d_in, int channels, int64_t n, const double* h_gains, float* d_out, void* stream) {
+  if (!d_in || !h_gains || !d_out || channels < 1 || channels > trc::kRemixMaxChannels || n < 1)
+    return fail(TRC_E_INVALID, "bad remix arguments");
+  trc::launch_remix(d_in, channels, n, h_gains, d_out, (cudaStream_t)stream);
+  g_launches += 1;
+  return check_launch(cudaGetLastError(), "remix");
+}
+
+int trc_resample(const float* d_in, int channels, int64_t n_in, int up, int down, int64_t half, const double* d_taps,
+                 int k_per_phase, int64_t n_out, float* d_out, void* stream) {
+  if (!d_in || !d_taps || !d_out || channels < 1 || channels > 65535 || n_in < 1 || n_out < 1 || up < 1 ||
+      down < 1 || half < 0 || k_per_phase < 1 || (int64_t)k_per_phase * up > (int64_t)1 << 26 ||
+      (n_out - 1) > (INT64_MAX - half) / down)
+    return fail(TRC_E_INVALID, "bad resample arguments");
+  trc::launch_resample(d_in, channels, n_in, up, down, half, d_taps, k_per_phase, n_out, d_out, (cudaStream_t)stream);
+  g_launches += 1;
+  return check_launch(cudaGetLastError(), "resample");
+}
+
 // ------------------------------------------------------------------------------------------------ per stage
 int trc_add_rmsnorm(trc_handle* h, float* d_X, const float* d_Y, void* d_out, int out_f32, int64_t rows, float eps,
                     void* stream) {

@@ -1,6 +1,7 @@
 // fp32 signal-processing kernels around the transformer: STFT, band split, row L2-norm, mask apply +
 // iSTFT, and the Hamming overlap-add of chunk outputs. All HBM-bound; each thread block owns whole
 // frames / rows so every global access is coalesced and every intermediate stays in shared memory.
+#include <algorithm>
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -358,6 +359,60 @@ void launch_chunk_ola(const float* chunks, int64_t clen, const int64_t* d_starts
   const int64_t per_block = 256 * kOlaPerThread;
   chunk_ola_kernel<<<(unsigned)((n + per_block - 1) / per_block), 256, 0, st>>>(chunks, clen, d_starts, n_chunks, w,
                                                                                  n, out);
+}
+
+// ------------------------------------------------------------------------------------------ remix / resample
+// Channel fold to stereo (audio.downmix_stereo / to_stereo, turbo_roformer/audio.py:35-68): one output
+// sample per thread and side, the channel sum in fp64 in channel order, rounded once to fp32.
+struct RemixGains {
+  double g[2][kRemixMaxChannels];
+};
+
+__global__ void __launch_bounds__(256) remix_kernel(const float* __restrict__ x, int channels, int64_t n,
+                                                    const RemixGains gains, float* __restrict__ y) {
+  const int side = blockIdx.y;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    double acc = 0.0;
+    for (int k = 0; k < channels; ++k) acc = fma(gains.g[side][k], (double)__ldg(x + (size_t)k * n + i), acc);
+    y[(size_t)side * n + i] = (float)acc;
+  }
+}
+
+// Rational-ratio polyphase FIR resampling (the role of audio.resample, turbo_roformer/audio.py:71-82):
+// output m sits at t = m * down + half on the up-sampled grid; its taps are column p = t % up of the
+// [K][up] table and its inputs x[j0 - k], j0 = t / up, k = 0..K-1 (zero outside [0, n_in)). One output
+// per thread: a warp's outputs read neighbouring inputs (coalesced) and scattered columns of one tap row
+// (L1/L2 resident). fp64 accumulation in k order, rounded once.
+__global__ void __launch_bounds__(256) resample_kernel(const float* __restrict__ x, int64_t n_in, int up, int down,
+                                                       int64_t half, const double* __restrict__ taps, int K,
+                                                       int64_t n_out, float* __restrict__ y) {
+  const float* xc = x + (size_t)blockIdx.y * n_in;
+  float* yc = y + (size_t)blockIdx.y * n_out;
+  for (int64_t m = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; m < n_out;
+       m += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = m * down + half;
+    const int64_t j0 = t / up;
+    const int p = (int)(t - j0 * up);
+    const int k0 = j0 >= n_in ? (int)min(j0 - n_in + 1, (int64_t)K) : 0;  // skip inputs past the end
+    const int k1 = (int)min((int64_t)K, j0 + 1);                           // and before the start
+    double acc = 0.0;
+    for (int k = k0; k < k1; ++k) acc = fma(__ldg(taps + (size_t)k * up + p), (double)__ldg(xc + (j0 - k)), acc);
+    yc[m] = (float)acc;
+  }
+}
+
+void launch_remix(const float* x, int channels, int64_t n, const double* gains, float* y, cudaStream_t st) {
+  RemixGains g;
+  for (int side = 0; side < 2; ++side)
+    for (int k = 0; k < kRemixMaxChannels; ++k) g.g[side][k] = k < channels ? gains[side * channels + k] : 0.0;
+  const unsigned blocks = (unsigned)std::min<int64_t>((n + 255) / 256, 148 * 16);
+  remix_kernel<<<dim3(blocks, 2), 256, 0, st>>>(x, channels, n, g, y);
+}
+
+void launch_resample(const float* x, int channels, int64_t n_in, int up, int down, int64_t half, const double* taps,
+                     int K, int64_t n_out, float* y, cudaStream_t st) {
+  const unsigned blocks = (unsigned)std::min<int64_t>((n_out + 255) / 256, 148 * 16);
+  resample_kernel<<<dim3(blocks, channels), 256, 0, st>>>(x, n_in, up, down, half, taps, K, n_out, y);
 }
 
 }  // namespace trc

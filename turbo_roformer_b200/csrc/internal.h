@@ -27,6 +27,10 @@ void launch_add_rmsnorm(float* X, const float* Y, void* out, int out_f32, int64_
 void launch_wait_timeout_selftest(int* err, cudaStream_t st);
 void launch_chunk_ola(const float* chunks, int64_t clen, const int64_t* d_starts, int n_chunks, const float* w,
                       int64_t n, float* out, cudaStream_t st);
+constexpr int kRemixMaxChannels = 16;
+void launch_remix(const float* x, int channels, int64_t n, const double* gains, float* y, cudaStream_t st);
+void launch_resample(const float* x, int channels, int64_t n_in, int up, int down, int64_t half, const double* taps,
+                     int K, int64_t n_out, float* y, cudaStream_t st);
 
 // pack.cu (unfused attention-layout helpers)
 void launch_rope_pack(int precision, const void* qkvg, const float* cos_tab, const float* sin_tab, int mode, int T,

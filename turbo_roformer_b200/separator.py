@@ -196,28 +196,59 @@ class Separator:
         later synchronises and raises any device-side error."""
         return overlap_add_cuda(self.net, x, self.chunk, overlap, batch=self.batch, progress=progress, check=check)
 
+    @staticmethod
+    def _pinned(x) -> torch.Tensor:
+        """A pinned float32 CPU tensor holding x (numpy or CPU tensor); a pinned tensor is used as is."""
+        if isinstance(x, torch.Tensor) and x.is_pinned() and x.dtype == torch.float32 and x.is_contiguous():
+            return x
+        a = np.ascontiguousarray(x.numpy() if isinstance(x, torch.Tensor) else x, dtype=np.float32)
+        src = torch.empty(a.shape, dtype=torch.float32, pin_memory=True)
+        src.numpy()[...] = a
+        return src
+
     @torch.inference_mode()
     def _submit_44k(self, x, overlap: float, progress, out: torch.Tensor | None) -> "SeparationJob":
         """separator.py:186-200 queued on the GPU without a host synchronisation.
 
         The samples are copied to the GPU once (from pinned memory: the caller's, or a pinned staging
-        copy of a numpy mix), the peak gain PEAK / max|x| (rounded from double to float32, as the host
-        code computes it) multiplies the mix and divides the instrumental on the device, the NaN/inf scan
-        is max|x| being finite (NaN propagates through the maximum), and one asynchronous copy returns
-        the instrumental into pinned host memory. ``x`` is (2, n) float32: numpy or a CPU tensor."""
+        copy of a numpy mix). ``x`` is (2, n) float32: numpy or a CPU tensor."""
         n0 = x.shape[1]
-        if isinstance(x, torch.Tensor) and x.is_pinned() and n0 >= self.chunk:
-            src = x
-        else:
-            xp = np.ascontiguousarray(self._pad_short(x.numpy() if isinstance(x, torch.Tensor) else x))
-            src = torch.empty(xp.shape, dtype=torch.float32, pin_memory=True)
-            src.numpy()[...] = xp
+        if not (isinstance(x, torch.Tensor) and x.is_pinned() and n0 >= self.chunk):
+            x = self._pad_short(x.numpy() if isinstance(x, torch.Tensor) else x)
+        src = self._pinned(x)
+        return self._submit_device(src.to(self.device, non_blocking=True), n0, overlap, progress, out, src)
+
+    @torch.inference_mode()
+    def _submit_resampled(self, x: np.ndarray, sr: int, overlap: float, progress) -> "SeparationJob":
+        """Any channel count and sample rate: the channel fold and both rate conversions on the GPU
+        (``resample.remix_device`` / ``resample_device``), the 44.1 kHz part as ``_submit_44k``.
+        The reference does these on the host (separator.py:214-230, audio.py:35-82)."""
+        from .resample import remix_device, resample_device
+
+        n = x.shape[1]
+        src = self._pinned(x)
+        xd = remix_device(src.to(self.device, non_blocking=True))
+        if sr != SR:
+            xd = resample_device(xd, sr, SR, length=max(1, round(n * SR / sr)))
+        n0 = xd.shape[1]
+        xd = torch.nn.functional.pad(xd, (0, self._padded_length(n0) - n0)).contiguous()
+        post = (lambda inst: resample_device(inst.contiguous(), SR, sr, length=n)) if sr != SR else None
+        out = torch.empty((2, n), dtype=torch.float32, pin_memory=True)
+        return self._submit_device(xd, n0, overlap, progress, out, src, post)
+
+    def _submit_device(self, xd: torch.Tensor, n0: int, overlap: float, progress, out: torch.Tensor | None,
+                       src: torch.Tensor, post=None) -> "SeparationJob":
+        """The part of separator.py:186-200 after the upload: ``xd`` (2, n) on the GPU, already padded;
+        the first n0 samples are the song. The peak gain PEAK / max|x| (rounded from double to float32,
+        as the host code computes it) multiplies the mix and divides the instrumental on the device, the
+        NaN/inf scan is max|x| being finite (NaN propagates through the maximum), and one asynchronous
+        copy returns the instrumental (through ``post`` if given) into pinned host memory."""
+        n_res = out.shape[1] if (post is not None and out is not None) else n0
         if out is None:
-            out = torch.empty((2, n0), dtype=torch.float32, pin_memory=True)
-        elif out.shape != (2, n0) or out.dtype != torch.float32 or not out.is_pinned() or not out.is_contiguous():
-            raise ValueError(f"out must be a contiguous pinned float32 CPU tensor of shape (2, {n0})")
+            out = torch.empty((2, n_res), dtype=torch.float32, pin_memory=True)
+        elif out.shape != (2, n_res) or out.dtype != torch.float32 or not out.is_pinned() or not out.is_contiguous():
+            raise ValueError(f"out must be a contiguous pinned float32 CPU tensor of shape (2, {n_res})")
         flags = torch.zeros(2, dtype=torch.int32, pin_memory=True)  # [device error word, non-finite input]
-        xd = src.to(self.device, non_blocking=True)
         peak = xd.abs().amax()
         gain = torch.where(peak > PEAK, (PEAK / peak.double()).float(), torch.ones((), device=xd.device))
         xd.mul_(gain)
@@ -227,6 +258,7 @@ class Separator:
         job = SeparationJob(self, out, flags)
         job._song = _Song(xd, starts, C, n0, gain, peak, torch.empty(len(starts), 2, self.net.output_length(C),
                                                                     device=xd.device, dtype=torch.float32), src)
+        job._song.post = post
         if C != self.chunk or progress is not None:
             # a short clip (its own chunk length) or a caller that follows the chunks: its own forwards
             run_chunks(self.net, xd, starts, C, self.batch, job._song.outs, progress, check=False)
@@ -259,12 +291,13 @@ class Separator:
         g = job._song
         inst = ola_device(g.outs, g.starts, g.C, g.n)
         inst.div_(g.gain)
-        job._out.copy_(inst[:, : g.n0], non_blocking=True)
+        res = inst[:, : g.n0] if g.post is None else g.post(inst[:, : g.n0])
+        job._out.copy_(res, non_blocking=True)
         job._flags[1:].copy_((~torch.isfinite(g.peak)).to(torch.int32).reshape(1), non_blocking=True)
         self.net.error_async(job._flags[:1])
         job._done = torch.cuda.Event()
         job._done.record(torch.cuda.current_stream(self.device))
-        job._keep = (g, inst)
+        job._keep = (g, inst, res)
         job._song = None
 
     def flush(self) -> None:
@@ -324,18 +357,14 @@ class Separator:
         if int(sr) <= 0:
             raise ValueError("sr must be positive")
         sr = int(sr)
-        x = audio.to_stereo(audio.as_channels_first(mix, finite=False))
-        n = x.shape[1]
-        if sr != SR:
-            audio.check_finite(x)
-            x = audio.resample(x, sr, SR, length=max(1, round(n * SR / sr)))
+        x = audio.as_channels_first(mix, finite=False)
         with self._lock:
             if self.threads:
                 torch.set_num_threads(int(self.threads))
-            inst = self._separate_44k(x, float(overlap), progress)
-        if sr != SR:
-            inst = audio.resample(inst, SR, sr, length=n)
-        return inst
+            if sr == SR and x.shape[0] == 2:
+                return self._separate_44k(x, float(overlap), progress)
+            # fold and rate conversion on the GPU around the 44.1 kHz model
+            return self._submit_resampled(x, sr, float(overlap), progress).result()
 
     def separate_file(
         self,
@@ -393,6 +422,7 @@ class _Song:
             xd, starts, C, n0, gain, peak, outs, src)
         self.n = xd.shape[1]
         self.left = len(starts)
+        self.post = None  # device transform of the instrumental before the copy back (rate conversion)
 
 
 class SeparationJob:
