@@ -42,8 +42,11 @@ extern "C" {
 typedef struct trc_handle trc_handle;
 
 /* Architecture of a single-stem stereo BS-RoFormer (turbo_roformer/model.py:181-245;
- * turbo_roformer/registry.py:49-69). Supported: dim 256, 8 heads x 64, depth-1 time/freq transformers,
- * mask_estimator_depth 2, power-of-two n_fft in [256, 4096] with win_length == n_fft, <= 64 bands. */
+ * turbo_roformer/registry.py:49-69). Supported: dim 128, 256, 384 or 512 (256 runs the fused epilogue
+ * kernels; the other widths run their residual branches as fp32 GEMMs followed by row norms, as the
+ * reference drops its fused kernels for them, fast.py:121-122), 8 heads x 64, depth-1 time/freq
+ * transformers, mask_estimator_depth 2, power-of-two n_fft in [256, 4096] with win_length == n_fft,
+ * <= 64 bands. */
 typedef struct trc_config {
   int dim;
   int depth;
@@ -76,7 +79,7 @@ int trc_forward(trc_handle* h, const float* d_audio, int batch, int64_t samples,
 int64_t trc_output_length(const trc_handle* h, int64_t samples);
 
 /* Replaces FastBSRoformer._transformer_cpp (turbo_roformer/fast.py:269-341): the 2*depth time/frequency
- * transformers alone on the fp32 residual stream d_X [batch * T * n_bands][256] (token order
+ * transformers alone on the fp32 residual stream d_X [batch * T * n_bands][dim] (token order
  * (batch, frame, band)), updated in place. Uses the handle's work buffers; asynchronous on `stream`. */
 int trc_transformer(trc_handle* h, float* d_X, int batch, int T, void* stream);
 

@@ -1,0 +1,47 @@
+"""Models whose width is not 256 (the other-checkpoint row: fast.py:121-122 drops the reference's fused
+kernels for them): the forward at widths 128, 384 and 512 against the fp32 oracle on the same weights."""
+
+from __future__ import annotations
+
+import dataclasses
+
+import pytest
+import torch
+
+from oracle import roformer_oracle as R
+from turbo_roformer_b200 import config as C
+from turbo_roformer_b200 import synthetic as S
+
+from .conftest import snr_db
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("dim", [128, 384, 512])
+def test_forward_other_widths_match_oracle(cuda_device, dim):
+    from turbo_roformer_b200.backend import CudaBSRoformer
+
+    cfg = dataclasses.replace(C.TINY, dim=dim)
+    sd = S.tiny_weights(cfg, seed=dim)
+    m = CudaBSRoformer(sd, cfg=cfg, device=0, precision="fp16")
+    for n, seed in ((cfg.chunk, 0), (5000, 1)):
+        x = torch.from_numpy(S.chunk_audio(n, seed=seed)).unsqueeze(0)
+        ref = R.forward(x, sd, cfg)[0].numpy()
+        y = m(x)[0].numpy()
+        assert y.shape == ref.shape
+        assert snr_db(ref, y) >= 50.0, (dim, n)
+    # batch invariance holds on the unfused path too
+    xs = torch.from_numpy(S.chunk_audio(cfg.chunk * 3, seed=5)).reshape(2, 3, -1).permute(1, 0, 2).contiguous().cuda()
+    yb = m.forward_device(xs)
+    y1 = m.forward_device(xs[1:2].contiguous())
+    torch.testing.assert_close(yb[1:2], y1, rtol=0, atol=0)
+
+
+def test_separator_runs_a_wide_model(cuda_device):
+    from turbo_roformer_b200.separator import Separator
+
+    cfg = dataclasses.replace(C.TINY, dim=384)
+    sep = Separator.from_module(S.tiny_weights(cfg, seed=3), cfg.stft_hop_length, cfg.dim_t, batch=2)
+    mix = S.chunk_audio(3 * cfg.chunk + 100, seed=4)
+    inst = sep.separate(mix)
+    assert inst.shape == mix.shape and torch.isfinite(torch.from_numpy(inst)).all()

@@ -203,6 +203,7 @@ struct trc_handle {
   // forward work buffers (sized for ws_B x ws_T)
   int ws_B = 0, ws_T = 0;
   DevBuf<float> xin, X, mask, frames;
+  DevBuf<float> Y;  // fp32 residual branch [rows][dim] (models whose width is not 256)
   DevBuf<uint16_t> bs_a;  // normalised, padded band inputs [rows][bs_kp]
   DevBuf<uint16_t> xn, Q, K, V, O, H;
   DevBuf<float> G;
@@ -364,7 +365,8 @@ int ensure_workspace(trc_handle* h, int B, int T) {
   const size_t hid = (size_t)(h->ff > h->hidden ? h->ff : h->hidden);
   int rc;
   if ((rc = h->xin.alloc(BT * h->width)) || (rc = h->mask.alloc(BT * h->width)) ||
-      (rc = h->frames.alloc(BT * 2 * h->n_fft)) || (rc = h->X.alloc(N * 256)) || (rc = h->xn.alloc(N * 256)) ||
+      (rc = h->frames.alloc(BT * 2 * h->n_fft)) || (rc = h->X.alloc(N * h->dim)) || (rc = h->xn.alloc(N * h->dim)) ||
+      (h->dim != 256 && (rc = h->Y.alloc(N * h->dim))) ||
       (rc = h->Q.alloc(N * 512)) || (rc = h->K.alloc(N * 512)) || (rc = h->V.alloc(N * 512)) ||
       (rc = h->O.alloc(N * 512)) || (rc = h->H.alloc(N * hid)) || (rc = h->G.alloc(N * 8)) ||
       (rc = h->bs_a.alloc(BT * h->bs_kp)))
@@ -423,10 +425,11 @@ int run_qkv(trc_handle* h, int layer, const void* xn, int B, int T, void* Q, voi
   LayerDev& lw = *h->layers[layer];
   CUtensorMap ma, mo[3];
   int rc;
-  GemmArgs a = dense_args(h, 1, 1544, 256);
+  const int D = h->dim;
+  GemmArgs a = dense_args(h, 1, 1544, D);
   if (mode == 0) {  // A rows: 128 consecutive frames of one band, xn viewed as (k, band, frame, batch)
-    const uint64_t dims[4] = {256, (uint64_t)F, (uint64_t)T, (uint64_t)B};
-    const uint64_t strides[3] = {512, (uint64_t)F * 512, (uint64_t)T * F * 512};
+    const uint64_t dims[4] = {(uint64_t)D, (uint64_t)F, (uint64_t)T, (uint64_t)B};
+    const uint64_t strides[3] = {(uint64_t)D * 2, (uint64_t)F * D * 2, (uint64_t)T * F * D * 2};
     const uint32_t box[4] = {64, 1, 128, 1};
     if ((rc = make_map_cached(h, &ma, xn, 4, dims, strides, box))) return rc;
     a.a_mode = trc::A_TIME_SEQ;
@@ -434,8 +437,8 @@ int run_qkv(trc_handle* h, int layer, const void* xn, int B, int T, void* Q, voi
     a.m_tiles = (T + 127) / 128;
     a.num_tiles = B * F * a.m_tiles * a.n_tiles;
   } else {  // A rows: two frames x 64 band slots, xn viewed as (k, band, frame)
-    const uint64_t dims[3] = {256, (uint64_t)F, (uint64_t)B * T};
-    const uint64_t strides[2] = {512, (uint64_t)F * 512};
+    const uint64_t dims[3] = {(uint64_t)D, (uint64_t)F, (uint64_t)B * T};
+    const uint64_t strides[2] = {(uint64_t)D * 2, (uint64_t)F * D * 2};
     const uint32_t box[3] = {64, 64, 2};
     if ((rc = make_map_cached(h, &ma, xn, 3, dims, strides, box))) return rc;
     a.a_mode = trc::A_FREQ_PAIR;
@@ -454,7 +457,10 @@ int run_qkv(trc_handle* h, int layer, const void* xn, int B, int T, void* Q, voi
   a.sin_tab = tab->sin_t.p;
   a.T = T;
   a.F = F;
-  return check_launch(trc::launch_gemm(trc::EPI_QKV, h->prec, ma, lw.m_wqkv, mo, a, h->num_sms, st), "qkv gemm");
+  // a 256-wide row block stays resident in shared memory for all 7 column tiles; wider ones stream with B
+  return check_launch(trc::launch_gemm(D == 256 ? trc::EPI_QKV : trc::EPI_QKVS, h->prec, ma, lw.m_wqkv, mo, a,
+                                       h->num_sms, st),
+                      "qkv gemm");
 }
 
 int run_attention(trc_handle* h, int mode, const void* Q, const void* K, const void* V, const float* G, void* O,
@@ -500,8 +506,35 @@ int run_attention(trc_handle* h, int mode, const void* Q, const void* K, const v
   return check_launch(trc::launch_attention(h->prec, mq, mk, mv, a, h->num_sms, st), "attention");
 }
 
+// Models whose width D is not 256: Y = A W^T (+ b) in fp32 through EPI_F32, then X += Y and
+// xn = X / max(|X|, 1e-12) by the row kernel (the unfused gemm + add_rmsnorm pair of kernels.cpp:543-586).
+int run_res_add(trc_handle* h, int layer, int which, const void* A, float* X, void* xn, int64_t rows, cudaStream_t st) {
+  LayerDev& lw = *h->layers[layer];
+  const int k = which == 0 ? 512 : h->ff;
+  const int D = h->dim;
+  CUtensorMap ma, mo[3];
+  int rc = map_2d_cached(h, &ma, A, (uint64_t)k, (uint64_t)rows, 128);
+  if (rc) return rc;
+  const uint64_t dims[2] = {(uint64_t)D, (uint64_t)rows};
+  const uint64_t st_y[1] = {(uint64_t)D * 4};
+  const uint32_t box_y[2] = {32, 32};
+  if ((rc = make_map_cached(h, &mo[0], h->Y.p, 2, dims, st_y, box_y, kMapF32))) return rc;
+  mo[1] = mo[0];
+  mo[2] = mo[0];
+  GemmArgs a = dense_args(h, rows, D, k);
+  a.out0 = h->Y.p;
+  a.bias = which == 0 ? nullptr : lw.b2.p;
+  if ((rc = check_launch(
+           trc::launch_gemm(trc::EPI_F32, h->prec, ma, which == 0 ? lw.m_wo : lw.m_w2, mo, a, h->num_sms, st),
+           "residual-branch gemm")))
+    return rc;
+  trc::launch_add_rmsnorm(X, h->Y.p, xn, 0, rows, 1e-12f, h->prec, D, st);
+  return check_launch(cudaGetLastError(), "add_rmsnorm");
+}
+
 int run_res_norm(trc_handle* h, int layer, int which, const void* A, float* X, void* xn, int64_t rows,
                  cudaStream_t st) {
+  if (h->dim != 256) return run_res_add(h, layer, which, A, X, xn, rows, st);
   LayerDev& lw = *h->layers[layer];
   const int k = which == 0 ? 512 : h->ff;
   CUtensorMap ma;
@@ -526,9 +559,16 @@ int run_res_norm(trc_handle* h, int layer, int which, const void* A, float* X, v
 
 // Fused feed-forward block: X += GELU(xn W1^T + b1) W2^T + b2, xn_out = X / max(|X|, 1e-12) (mlp.cuh).
 // xn_out may be xn itself: a row block's output is written after every read of that block's input.
+int run_gelu(trc_handle* h, int layer, const void* xn, void* H, int64_t rows, cudaStream_t st);
+
 int run_ffn(trc_handle* h, int layer, const void* xn, float* X, void* xn_out, int64_t rows, cudaStream_t st) {
   LayerDev& lw = *h->layers[layer];
-  if (h->ff % 128 || h->dim != 256) return fail(TRC_E_INVALID, "the fused feed-forward needs dim 256, hidden % 128 == 0");
+  if (h->dim != 256) {  // unfused: H = GELU(xn W1^T + b1), then the residual branch H W2^T + b2
+    int rc = run_gelu(h, layer, xn, h->H.p, rows, st);
+    if (rc) return rc;
+    return run_res_add(h, layer, 1, h->H.p, X, xn_out, rows, st);
+  }
+  if (h->ff % 128) return fail(TRC_E_INVALID, "the fused feed-forward needs a hidden width that is a multiple of 128");
   CUtensorMap ma, mx, mxn;
   int rc;
   if ((rc = map_2d_cached(h, &ma, xn, 256, (uint64_t)rows, 128))) return rc;
@@ -551,13 +591,13 @@ int run_ffn(trc_handle* h, int layer, const void* xn, float* X, void* xn_out, in
 int run_gelu(trc_handle* h, int layer, const void* xn, void* H, int64_t rows, cudaStream_t st) {
   LayerDev& lw = *h->layers[layer];
   CUtensorMap ma;
-  int rc = map_2d_cached(h, &ma, xn, 256, (uint64_t)rows, 128);
+  int rc = map_2d_cached(h, &ma, xn, (uint64_t)h->dim, (uint64_t)rows, 128);
   if (rc) return rc;
   CUtensorMap mo[3];
   if ((rc = map_2d_cached(h, &mo[0], H, (uint64_t)h->ff, (uint64_t)rows, 128))) return rc;
   mo[1] = mo[0];
   mo[2] = mo[0];
-  GemmArgs a = dense_args(h, rows, h->ff, 256);
+  GemmArgs a = dense_args(h, rows, h->ff, h->dim);
   a.out0 = H;
   a.bias = lw.b1.p;
   a.ld_out = h->ff;
@@ -572,8 +612,8 @@ int run_mask(trc_handle* h, const void* xn, int B, int T, float* mask, void* hid
   // layer 1: per band, tanh(xn_band W1'^T + b1) -> hid [band][BT][hidden]
   {
     CUtensorMap ma;
-    const uint64_t dims[3] = {256, (uint64_t)F, (uint64_t)BT};
-    const uint64_t strides[2] = {512, (uint64_t)F * 512};
+    const uint64_t dims[3] = {(uint64_t)h->dim, (uint64_t)F, (uint64_t)BT};
+    const uint64_t strides[2] = {(uint64_t)h->dim * 2, (uint64_t)F * h->dim * 2};
     const uint32_t box[3] = {64, 1, 128};
     if ((rc = make_map_cached(h, &ma, xn, 3, dims, strides, box))) return rc;
     CUtensorMap mo[3];
@@ -587,7 +627,7 @@ int run_mask(trc_handle* h, const void* xn, int B, int T, float* mask, void* hid
     }
     GemmArgs a;
     std::memset(&a, 0, sizeof(a));
-    a.k_blocks = 4;
+    a.k_blocks = h->dim / 64;
     a.a_mode = trc::A_GROUP_ROWS;
     a.M = BT;
     a.n_groups = F;
@@ -650,6 +690,45 @@ int run_mask(trc_handle* h, const void* xn, int B, int T, float* mask, void* hid
 
 int frames_for(const trc_handle* h, int64_t samples) { return (int)(1 + samples / h->hop); }
 
+// Band split for models whose width D is not 256: the grouped GEMM writes X = A W'^T + b through EPI_F32
+// (ceil(D / 256) column tiles per band), then the row kernel makes xn.
+int run_band_split_wide(trc_handle* h, const CUtensorMap& ma, int rows, float* X, void* xn, cudaStream_t st) {
+  const int nb = h->nb, D = h->dim;
+  CUtensorMap mo[3];
+  const uint64_t dims[3] = {(uint64_t)D, (uint64_t)nb, (uint64_t)rows};
+  const uint64_t st_x[2] = {(uint64_t)D * 4, (uint64_t)nb * D * 4};
+  const uint32_t box_x[3] = {32, 1, 32};
+  int rc;
+  if ((rc = make_map_cached(h, &mo[0], X, 3, dims, st_x, box_x, kMapF32))) return rc;
+  mo[1] = mo[0];
+  mo[2] = mo[0];
+  GemmArgs a;
+  std::memset(&a, 0, sizeof(a));
+  a.a_mode = trc::A_BAND;
+  a.M = rows;
+  a.F = nb;
+  a.n_groups = nb;
+  const int mt = (rows + 127) / 128, nt = (D + 255) / 256;
+  for (int g = 0; g < nb; ++g) {
+    a.g_tile_start[g] = g * mt * nt;
+    a.g_ntiles[g] = nt;
+    a.g_brow[g] = 0;
+    a.g_ncols[g] = D;
+    a.g_koff[g] = h->pad_off[g];
+    a.g_kblocks[g] = (h->pad_off[g + 1] - h->pad_off[g]) / 64;
+  }
+  a.g_tile_start[nb] = nb * mt * nt;
+  a.num_tiles = nb * mt * nt;
+  a.out0 = X;
+  a.bias = h->bs_bias.p;
+  a.bias_gstride = D;
+  a.err = h->err.p;
+  if ((rc = check_launch(trc::launch_gemm(trc::EPI_F32, h->prec, ma, h->m_bs_w, mo, a, h->num_sms, st), "band split")))
+    return rc;
+  trc::launch_rownorm(X, xn, (int64_t)rows * nb, 1e-12f, h->prec, D, st);
+  return check_launch(cudaGetLastError(), "norm");
+}
+
 // Band split (model.py:147-155) + the transformers' first norm: the band-pack kernel normalises and pads
 // each band's inputs into h->bs_a (16-bit), then one grouped GEMM over the bands writes X = A W'^T + b
 // [rows][nb][256] fp32 and xn = X / max(|X|, 1e-12) (16-bit).
@@ -661,6 +740,7 @@ int run_band_split(trc_handle* h, const float* xin, int B, int T, float* X, void
   if ((rc = check_launch(cudaGetLastError(), "band pack"))) return rc;
   CUtensorMap ma;
   if ((rc = map_2d_cached(h, &ma, h->bs_a.p, h->bs_kp, rows, 128))) return rc;
+  if (h->dim != 256) return run_band_split_wide(h, ma, rows, X, xn, st);
   // X (fp32) and xn (16-bit) as 3-D views (256, bands, rows), stored by TMA in boxes of 32 rows of one
   // band: 32 columns of X, 64 of xn
   CUtensorMap mo[3];
@@ -707,7 +787,7 @@ int run_transformers(trc_handle* h, float* X, int batch, int T, cudaStream_t st,
   if (!xn_ready) {
     {
       Section sec(h, "norm", st);
-      trc::launch_rownorm(X, h->xn.p, rows, 1e-12f, h->prec, st);
+      trc::launch_rownorm(X, h->xn.p, rows, 1e-12f, h->prec, h->dim, st);
     }
     if ((rc = check_launch(cudaGetLastError(), "norm"))) return rc;
   }
@@ -743,7 +823,8 @@ const char* trc_last_error(void) { return g_last_error.c_str(); }
 int trc_create(const trc_config* cfg, int device, trc_handle** out) {
   if (!cfg || !out) return fail(TRC_E_INVALID, "null argument");
   *out = nullptr;
-  if (cfg->dim != 256) return fail(TRC_E_INVALID, "only dim=256 is supported");
+  if (cfg->dim != 128 && cfg->dim != 256 && cfg->dim != 384 && cfg->dim != 512)
+    return fail(TRC_E_INVALID, "dim must be 128, 256, 384 or 512");
   if (cfg->heads != 8 || cfg->dim_head != 64) return fail(TRC_E_INVALID, "only heads=8, dim_head=64 is supported");
   if (cfg->depth < 1) return fail(TRC_E_INVALID, "depth must be >= 1");
   const int n = cfg->n_fft;
@@ -775,8 +856,9 @@ int trc_create(const trc_config* cfg, int device, trc_handle** out) {
   h->device = device;
   TRC_CUDA(cudaDeviceGetAttribute(&h->num_sms, cudaDevAttrMultiProcessorCount, device));
   h->depth = cfg->depth;
-  h->ff = 256 * cfg->ff_mult;
-  h->hidden = 256 * cfg->mlp_expansion_factor;
+  h->dim = cfg->dim;
+  h->ff = cfg->dim * cfg->ff_mult;
+  h->hidden = cfg->dim * cfg->mlp_expansion_factor;
   if (h->ff % 256 || h->hidden % 256) return fail(TRC_E_INVALID, "ff and mask hidden widths must be multiples of 256");
   h->nb = cfg->n_bands;
   h->n_fft = n;
@@ -807,8 +889,8 @@ int trc_set_param(trc_handle* h, const char* name, const float* data, int64_t nu
 int trc_prepare(trc_handle* h) {
   if (!h) return fail(TRC_E_INVALID, "null handle");
   TRC_CUDA(cudaSetDevice(h->device));
-  const int d = 256, ff = h->ff, prec = h->prec;
-  const float sqrt_d = 16.0f;  // sqrt(256), exact
+  const int d = h->dim, ff = h->ff, prec = h->prec;
+  const float sqrt_d = (float)std::sqrt((double)d);  // 16 exactly for the 256-wide models
   int rc;
   h->layers.clear();
   for (int i = 0; i < h->depth; ++i) {
@@ -1148,7 +1230,7 @@ int trc_add_rmsnorm(trc_handle* h, float* d_X, const float* d_Y, void* d_out, in
   TRC_REQUIRE_PREPARED(h);
   if (!d_X || !d_out || rows < 0) return fail(TRC_E_INVALID, "bad add_rmsnorm arguments");
   Section sec(h, "norm", (cudaStream_t)stream);
-  trc::launch_add_rmsnorm(d_X, d_Y, d_out, out_f32, rows, eps, h->prec, (cudaStream_t)stream);
+  trc::launch_add_rmsnorm(d_X, d_Y, d_out, out_f32, rows, eps, h->prec, h->dim, (cudaStream_t)stream);
   return check_launch(cudaGetLastError(), "add_rmsnorm");
 }
 

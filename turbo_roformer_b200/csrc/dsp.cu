@@ -240,6 +240,55 @@ __global__ void add_rmsnorm_kernel(float* __restrict__ X, const float* __restric
   }
 }
 
+// Rows of any width 128 * NV (models whose width is not 256): X (+)= Y, out = X / max(|X|, eps), one warp
+// per row, lane l holding float4s l, l + 32, ... of the row.
+template <typename TOut, int NV>
+__global__ void add_rmsnorm_d_kernel(float* __restrict__ X, const float* __restrict__ Y, void* __restrict__ out,
+                                     int out_f32, int64_t rows, float eps) {
+  constexpr int D = 128 * NV;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  float4* xr = reinterpret_cast<float4*>(X + row * D);
+  float4 v[NV];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    v[i] = xr[i * 32 + lane];
+    if (Y) {
+      const float4 y = reinterpret_cast<const float4*>(Y + row * D)[i * 32 + lane];
+      v[i].x += y.x; v[i].y += y.y; v[i].z += y.z; v[i].w += y.w;
+      xr[i * 32 + lane] = v[i];
+    }
+    ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+  }
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, d);
+  const float inv = 1.0f / fmaxf(sqrtf(ss), eps);
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    if (out_f32)
+      reinterpret_cast<float4*>(static_cast<float*>(out) + row * D)[i * 32 + lane] =
+          make_float4(v[i].x * inv, v[i].y * inv, v[i].z * inv, v[i].w * inv);
+    else
+      reinterpret_cast<uint2*>(static_cast<TOut*>(out) + row * D)[i * 32 + lane] =
+          make_uint2(OperandType<TOut>::pack2(v[i].x * inv, v[i].y * inv),
+                     OperandType<TOut>::pack2(v[i].z * inv, v[i].w * inv));
+  }
+}
+
+template <typename TOut>
+void launch_add_rmsnorm_d(float* X, const float* Y, void* out, int out_f32, int64_t rows, float eps, int dim,
+                          cudaStream_t st) {
+  const unsigned blocks = (unsigned)((rows + 7) / 8);
+  switch (dim) {
+    case 128: add_rmsnorm_d_kernel<TOut, 1><<<blocks, 256, 0, st>>>(X, Y, out, out_f32, rows, eps); break;
+    case 384: add_rmsnorm_d_kernel<TOut, 3><<<blocks, 256, 0, st>>>(X, Y, out, out_f32, rows, eps); break;
+    case 512: add_rmsnorm_d_kernel<TOut, 4><<<blocks, 256, 0, st>>>(X, Y, out, out_f32, rows, eps); break;
+    default: add_rmsnorm_d_kernel<TOut, 2><<<blocks, 256, 0, st>>>(X, Y, out, out_f32, rows, eps); break;
+  }
+}
+
 // Hamming-weighted overlap-add of chunk outputs (turbo_roformer/chunking.py:54-61). For each sample the
 // covering chunks form a contiguous range of the (increasing) starts; they are summed in start order
 // with separately rounded multiply and add, so the result equals the reference's sequential
@@ -320,7 +369,14 @@ void launch_band_pack(const float* xin, int width, int rows, int nbands, const i
         <<<rows, 256, 0, st>>>(xin, width, nbands, band_off, pad_off, kp, static_cast<__nv_bfloat16*>(a));
 }
 
-void launch_rownorm(const float* X, void* xn, int64_t rows, float eps, int precision, cudaStream_t st) {
+void launch_rownorm(const float* X, void* xn, int64_t rows, float eps, int precision, int dim, cudaStream_t st) {
+  if (dim != 256) {
+    if (precision == 0)
+      launch_add_rmsnorm_d<__half>(const_cast<float*>(X), nullptr, xn, 0, rows, eps, dim, st);
+    else
+      launch_add_rmsnorm_d<__nv_bfloat16>(const_cast<float*>(X), nullptr, xn, 0, rows, eps, dim, st);
+    return;
+  }
   const unsigned blocks = (unsigned)((rows + 7) / 8);
   if (precision == 0)
     rownorm_kernel<__half><<<blocks, 256, 0, st>>>(X, static_cast<__half*>(xn), rows, eps);
@@ -329,7 +385,14 @@ void launch_rownorm(const float* X, void* xn, int64_t rows, float eps, int preci
 }
 
 void launch_add_rmsnorm(float* X, const float* Y, void* out, int out_f32, int64_t rows, float eps, int precision,
-                        cudaStream_t st) {
+                        int dim, cudaStream_t st) {
+  if (dim != 256) {
+    if (precision == 0)
+      launch_add_rmsnorm_d<__half>(X, Y, out, out_f32, rows, eps, dim, st);
+    else
+      launch_add_rmsnorm_d<__nv_bfloat16>(X, Y, out, out_f32, rows, eps, dim, st);
+    return;
+  }
   const unsigned blocks = (unsigned)((rows + 7) / 8);
   if (precision == 0)
     add_rmsnorm_kernel<__half><<<blocks, 256, 0, st>>>(X, Y, out, out_f32, rows, eps);

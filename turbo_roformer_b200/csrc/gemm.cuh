@@ -17,13 +17,20 @@
 //   EPI_MASK_GLU  mask MLP layer 2 + GLU (fast.py:355-357): a * sigmoid(g), with (a, g) rows interleaved
 //   EPI_BAND      band split (model.py:147-155): X = acc + b per band, and the transformers' first norm
 //                 xn = X / max(|X|, eps) (kernels.cpp:102-137) in the same pass
+//   EPI_F32       Y = acc + b in fp32 (2-D, or 3-D per group): the unfused residual branch for models whose
+//                 width is not 256 (the norm then runs as add_rmsnorm / rownorm)
+//   EPI_QKVS      EPI_QKV with the A tile streamed with B (K other than 256: the resident tile would not fit)
 #pragma once
 
 #include "sm100.cuh"
 
 namespace trc {
 
-enum EpiKind : int { EPI_QKV = 0, EPI_RESNORM = 1, EPI_GELU = 2, EPI_MASK_TANH = 3, EPI_MASK_GLU = 4, EPI_BAND = 5 };
+enum EpiKind : int {
+  EPI_QKV = 0, EPI_RESNORM = 1, EPI_GELU = 2, EPI_MASK_TANH = 3, EPI_MASK_GLU = 4, EPI_BAND = 5, EPI_F32 = 6,
+  EPI_QKVS = 7
+};
+__host__ __device__ constexpr bool is_qkv(int epi) { return epi == EPI_QKV || epi == EPI_QKVS; }
 
 // How a tile's 128 A rows are addressed.
 enum AMode : int {
@@ -67,6 +74,7 @@ struct GemmArgs {
   void* out2;
   void* out3;
   const float* bias;   // indexed by B row (nullptr = none)
+  int bias_gstride;    // EPI_F32: bias of group g starts at bias + g * bias_gstride
   const float* bias2;  // qkv: gate bias [8]
   const float* cos_tab;
   const float* sin_tab;
@@ -656,6 +664,48 @@ __device__ __forceinline__ bool epi_band(const GemmArgs& a, const TileCoord& tc,
   return true;
 }
 
+// Plain fp32 output (EPI_F32): Y = acc + b. Each epilogue warp owns 32 rows x its half of the columns and
+// two 4 KB boxes (32 x 32 fp32, 128-byte swizzle), stored by TMA into Y, 2-D (N, rows) or for grouped
+// GEMMs 3-D (N, groups, rows); chunks at or past the tile's valid width are skipped.
+template <int BN>
+__device__ __forceinline__ void epi_f32(const GemmArgs& a, const TileCoord& tc, EpiCtx& e, uint8_t* box,
+                                        const CUtensorMap* map_y) {
+  const int lane = e.lane;
+  const int row0 = tc.m0 + e.quarter * 32;
+  const bool live = row0 < a.M;
+  const int swz = lane & 7;
+  const float* bias = a.bias ? a.bias + (size_t)tc.group * a.bias_gstride + tc.n0 : nullptr;
+  if (lane == 0) bulk_wait_read<0>();  // the previous tile's stores have read both boxes
+  __syncwarp();
+#pragma unroll 1
+  for (int c = 0; c < BN / 64; ++c) {
+    const int col = e.hf * (BN / 2) + c * 32;
+    if (col >= tc.n_valid) break;  // uniform over the warp
+    uint8_t* rowp = box + (c & 1) * kResBoxBytes + lane * 128;
+    if (c >= 2) {  // the store from this box two chunks ago has read it
+      if (lane == 0) bulk_wait_read<1>();
+      __syncwarp();
+    }
+    float v[32];
+    tmem_ld32(e.taddr + col, v);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float4 b = bias ? __ldg(reinterpret_cast<const float4*>(bias + col) + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+      *reinterpret_cast<float4*>(rowp + ((q ^ swz) << 4)) =
+          make_float4(v[4 * q] + b.x, v[4 * q + 1] + b.y, v[4 * q + 2] + b.z, v[4 * q + 3] + b.w);
+    }
+    fence_async_smem();
+    __syncwarp();
+    if (lane == 0 && live) {
+      if (a.n_groups > 0)
+        tma_store_3d(map_y, box + (c & 1) * kResBoxBytes, tc.n0 + col, tc.group, row0);
+      else
+        tma_store_2d(map_y, box + (c & 1) * kResBoxBytes, tc.n0 + col, row0);
+      bulk_commit();
+    }
+  }
+}
+
 // ------------------------------------------------------------------------------------------------ kernel
 template <int BN, int STAGES, int EPI>
 struct GemmSmem {
@@ -671,7 +721,7 @@ struct GemmSmem {
   static constexpr int kOutBytes = 2 * kSlabsPerHalf * kSlabBytes;
   static_assert(EPI != EPI_RESNORM || kEpiWarps * 2 * kResBoxBytes <= kOutBytes, "residual-norm boxes must fit");
   static constexpr int kTabOffset = kOutOffset + kOutBytes;  // rotary rows (qkv only)
-  static constexpr int kRsOffset = kTabOffset + (EPI == EPI_QKV ? kTabBytes : 0);  // row sums (norm epilogues)
+  static constexpr int kRsOffset = kTabOffset + (is_qkv(EPI) ? kTabBytes : 0);  // row sums (norm epilogues)
   static constexpr int kBarOffset = kRsOffset + (EPI == EPI_RESNORM || EPI == EPI_BAND ? 2 * 256 * 4 : 0);
   static constexpr int kBytes = kBarOffset + 256 + 1024;  // + barriers + alignment slack
   static_assert(kBytes <= 232448, "shared memory per CTA");
@@ -892,7 +942,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int buf = local & 1;
       const uint32_t use = (uint32_t)(local >> 1);
       if constexpr (EPI == EPI_RESNORM) resnorm_prefetch(args, tc, e, rst, &map_o0);  // overlaps this tile's MMAs
-      if constexpr (EPI == EPI_QKV) {
+      if constexpr (is_qkv(EPI)) {
         // the row block's rotary rows, staged while its first tile's MMAs run: time mode once per row
         // block (frames m0..m0+127), freq mode once per CTA (bands 0..63 for every block)
         if (u == 0 && (args.a_mode == A_TIME_SEQ || local == 0)) {
@@ -909,7 +959,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       tc_fence_after();
       e.taddr = tmem_base + (uint32_t)(buf * BN) + ((uint32_t)(e.quarter * 32) << 16);
-      if constexpr (EPI == EPI_QKV) {
+      if constexpr (is_qkv(EPI)) {
         epi_qkv<BN, TIn>(args, tc, e, &map_o0, &map_o1, &map_o2);
       } else if constexpr (EPI == EPI_RESNORM) {
         const bool ok2 = epi_resnorm<BN, TIn>(args, tc, e, rst, &map_o0, &map_o1,
@@ -922,6 +972,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         epi_act<BN, TIn>(args, tc, e, &map_o0, false);
       } else if constexpr (EPI == EPI_MASK_TANH) {
         epi_act<BN, TIn>(args, tc, e, &map_o0, true);
+      } else if constexpr (EPI == EPI_F32) {
+        epi_f32<BN>(args, tc, e, rst.box, &map_o0);
       } else if constexpr (EPI == EPI_BAND) {
         if (!epi_band<BN, TIn>(args, tc, e, rst.box, &map_o0, &map_o1, reinterpret_cast<float*>(smem + S::kRsOffset),
                                local)) {
@@ -935,7 +987,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_arrive(&acc_empty[buf]);
     }
     }
-    if constexpr (EPI == EPI_RESNORM || EPI == EPI_BAND) {
+    if constexpr (EPI == EPI_RESNORM || EPI == EPI_BAND || EPI == EPI_F32) {
       if constexpr (EPI == EPI_RESNORM) resnorm_drain(e, rst);
       if (lane == 0) bulk_wait<0>();  // this warp's stores have completed
     } else {

@@ -30,7 +30,8 @@ constexpr int kStages = 3;
 template <int EPI, typename T>
 cudaError_t launch_gemm_t(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap* mo, const GemmArgs& args,
                           int num_sms, cudaStream_t st) {
-  constexpr int kSt = EPI == EPI_QKV ? 2 : kStages;  // qkv: resident A tile + rotary rows take the space
+  // qkv: resident A tile (or streamed A, EPI_QKVS) + rotary rows take the space
+  constexpr int kSt = is_qkv(EPI) ? 2 : kStages;
   using S = GemmSmem<kBN, kSt, EPI>;
   auto kern = gemm_kernel<kBN, kSt, EPI, T>;
   static std::atomic<unsigned long long> done{0};  // one per <EPI, T> instantiation
@@ -52,6 +53,8 @@ cudaError_t launch_gemm_p(int epi, const CUtensorMap& ma, const CUtensorMap& mb,
     case EPI_MASK_TANH: return launch_gemm_t<EPI_MASK_TANH, T>(ma, mb, mo, args, num_sms, st);
     case EPI_MASK_GLU: return launch_gemm_t<EPI_MASK_GLU, T>(ma, mb, mo, args, num_sms, st);
     case EPI_BAND: return launch_gemm_t<EPI_BAND, T>(ma, mb, mo, args, num_sms, st);
+    case EPI_F32: return launch_gemm_t<EPI_F32, T>(ma, mb, mo, args, num_sms, st);
+    case EPI_QKVS: return launch_gemm_t<EPI_QKVS, T>(ma, mb, mo, args, num_sms, st);
     default: return cudaErrorInvalidValue;
   }
 }
