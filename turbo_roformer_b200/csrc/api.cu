@@ -18,6 +18,7 @@
 
 #include "../../include/trcuda.h"
 #include "attention.cuh"
+#include "attention_time.cuh"
 #include "gemm.cuh"
 #include "internal.h"
 #include "mlp.cuh"
@@ -480,8 +481,8 @@ int run_attention(trc_handle* h, int mode, const void* Q, const void* K, const v
     a.L = T;
     a.BH = B * F * 8;
     const int q_tiles = (T + 127) / 128;
-    a.q_pairs = (q_tiles + 1) / 2;
-    a.n_kv = q_tiles;
+    a.q_pairs = (q_tiles + trc::kTaTiles - 1) / trc::kTaTiles;  // items of three query tiles
+    a.n_kv = (T + 63) / 64;                                        // 64-key steps
     a.num_items = a.BH * a.q_pairs;
     box[0] = 64; box[1] = 128; box[2] = 1;
   } else {
@@ -500,8 +501,10 @@ int run_attention(trc_handle* h, int mode, const void* Q, const void* K, const v
   strides[1] = (uint64_t)a.L * 128;
   CUtensorMap mq, mk, mv;
   int rc;
-  if ((rc = make_map_cached(h, &mq, Q, 3, dims, strides, box)) || (rc = make_map_cached(h, &mk, K, 3, dims, strides, box)) ||
-      (rc = make_map_cached(h, &mv, V, 3, dims, strides, box)))
+  // time mode: Q in 128-row boxes, K and V in 64-row key tiles
+  const uint32_t kvbox[3] = {box[0], mode == 0 ? 64u : box[1], box[2]};
+  if ((rc = make_map_cached(h, &mq, Q, 3, dims, strides, box)) || (rc = make_map_cached(h, &mk, K, 3, dims, strides, kvbox)) ||
+      (rc = make_map_cached(h, &mv, V, 3, dims, strides, kvbox)))
     return rc;
   return check_launch(trc::launch_attention(h->prec, mq, mk, mv, a, h->num_sms, st), "attention");
 }

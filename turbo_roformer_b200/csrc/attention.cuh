@@ -1,36 +1,23 @@
-// Exact-softmax gated attention on tcgen05 (flash-style, online softmax with exact rescaling).
+// Frequency-mode attention (sequences over the bands of one frame and head) on tcgen05, and what the
+// time-mode kernel (attention_time.cuh) shares with it: the argument block, the TMEM/shared layouts'
+// helpers, the FMA-pipe exponential and the rescale threshold.
 //
-// Replaces the reference's AVX-512 `attention` kernel (LoggeL/turbo-roformer
+// Replaces the reference's AVX-512 `attention` kernel for mode 1 (LoggeL/turbo-roformer
 // src/turbo_roformer/csrc/kernels.cpp:255-388): per (sequence, head) S = Q K^T (scale folded into W_q),
 // softmax over the keys, O = P V, then x sigmoid gate, head merge and scatter back to token order.
-// The reference keeps whole score rows (two passes); here a CTA owns two 128-row query tiles (A, B)
-// and streams 128-key tiles:
-//   * S = Q K^T (both operands in shared memory) lands in TMEM. The softmax warps of the tile read the
-//     whole score row into registers at once, which frees the S columns: the next key tile's S is
-//     issued right then and runs on the tensor core while this tile's exponentials are computed.
-//   * Unnormalised 16-bit P goes to its own TMEM columns and the tensor core computes O += P V with P
-//     read straight from TMEM (no shared-memory round trip for P). O accumulates in TMEM.
-//   * The running row maximum is only raised when a tile's maximum exceeds it by more than 2^8 (then O
-//     and the row sum are rescaled in place); P <= 2^8 keeps 16-bit P exact enough and the final O / l
-//     is the exact softmax average.
-//   * Each query tile has its own MMA-issuing thread (warps 1 and 2), so the two tiles' products are
-//     issued independently: next S once the softmax has taken the previous one, P V once P is written.
-//   * At head dim 64 the exponentials, not the products, set the pace (16 ex2 per clock per SM on the
-//     MUFU pipe against 8192 tensor flops): one key pair in four is exponentiated by a polynomial on the
-//     FMA pipe instead (ex2_poly2), and the softmax warps take the registers the TMA / MMA warps do not
-//     need (setmaxnreg), so the whole score row and its packed P fit without spills.
-//   * Persistent CTAs walk the work items; Q is double buffered so the next item's first products
-//     start while the current item's epilogue runs.
-//
-// Layout: Q, K, V are [BH, L, 64] 16-bit, row-major, unpadded; the 3-D TMA maps zero-fill rows >= L.
-//   time mode (mode 0): sequences = (batch, band, head), L = T frames; an item = one sequence and two
-//                       consecutive 128-row query tiles; every key tile serves both query tiles.
-//   freq mode (mode 1): sequences = (batch, frame, head), L = bands <= 64; a query tile holds two
-//                       sequences (block-diagonal mask), an item = four sequences, each tile has its own
-//                       single key tile.
-// Roles (384 threads, three warpgroups): warp 0 TMA, warp 1 MMA issuer of tile A + TMEM owner, warp 2 MMA
-// issuer of tile B, warp 3 idle (warps 0-3 release registers); warps 4-7 softmax + epilogue of tile A,
-// warps 8-11 of tile B (thread = query row; warp w reads TMEM lanes 32 (w % 4) ..).
+// Sequences are L = bands <= 64 long, so one 128-row query tile holds two sequences (block-diagonal
+// mask: a row reads only the 64 score columns of its own sequence) and has a single 128-key tile:
+//   * S = Q K^T (both operands in shared memory) lands in TMEM; the softmax warps read their row's 64
+//     scores, write 16-bit P to its own TMEM columns (zeros for the other sequence's keys), and the tensor
+//     core computes O = P V with P read straight from TMEM. One key tile per item: no rescaling.
+//   * A CTA owns two query tiles (A, B), each with its own key stage and MMA-issuing thread (warps 1, 2);
+//     an item is four sequences (two per tile). Persistent CTAs; Q double buffered; each item's epilogue
+//     (gate / l, store) is deferred to the next item's step, after its P is written.
+// Layout: Q, K, V are [BH, L, 64] 16-bit, row-major, unpadded; the 3-D TMA maps (box 64 rows x 2
+// sequences) zero-fill rows >= L.
+// Roles (384 threads): warp 0 TMA, warp 1 MMA issuer of tile A + TMEM owner, warp 2 MMA issuer of tile B,
+// warp 3 idle; warps 4-7 softmax + epilogue of tile A, warps 8-11 of tile B (thread = query row; warp w
+// reads TMEM lanes 32 (w % 4) ..).
 #pragma once
 
 #include "gemm.cuh"  // store32
@@ -39,12 +26,6 @@
 namespace trc {
 
 constexpr int kAttnThreads = 384;
-// Time mode: registers per thread after setmaxnreg for warps 0-3 and for the softmax warpgroups. The
-// launch gives every thread the same count R (168 at 384 threads); the split needs
-// 4 * 32 * kAttnRegsLow + 8 * 32 * kAttnRegsHigh <= 384 * R, or the increase would wait forever
-// (launch_attention checks R before every time-mode launch).
-constexpr int kAttnRegsLow = 56;
-constexpr int kAttnRegsHigh = 216;
 // Key/value stages. Frequency mode loads one stage per tile and item (tile A, tile B, tile A, ...): with an
 // even stage count, stage (2 item + tile) % kAttnKvStages is only ever used by that one tile, so each
 // tile's MMA issuer waits on every phase of its stages in order. With an odd count the tiles would share
@@ -55,8 +36,8 @@ static_assert(kAttnKvStages % 2 == 0, "frequency mode needs per-tile stages");
 
 struct AttnArgs {
   int num_items;  // work items
-  int q_pairs;    // time: query-tile pairs per sequence
-  int n_kv;       // time: key tiles per sequence
+  int q_pairs;    // time: items (groups of three 128-row query tiles) per sequence
+  int n_kv;       // time: 64-key steps per item
   int L;          // valid length of every sequence
   int BH;         // number of sequences
   int mode;       // 0 time, 1 freq
@@ -102,11 +83,9 @@ __device__ __forceinline__ float2 ex2_poly2(float2 x) {
                      __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
 }
 
-// kFreq: frequency mode (compiled separately, so each mode gets its own register allocation); it must
-// equal args.mode == 1.
-template <typename TIn, bool kFreq>
+template <typename TIn>
 __global__ void __launch_bounds__(kAttnThreads, 1)
-    attention_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+    attention_freq_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                      const __grid_constant__ CUtensorMap map_v, const __grid_constant__ AttnArgs args) {
   using S = AttnSmem;
   extern __shared__ uint8_t smem_raw[];
@@ -127,9 +106,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  constexpr bool freq = kFreq;
-  const int nsteps = freq ? 1 : args.n_kv;       // key tiles per query tile and item
-  const int kv_per_item = freq ? 2 : args.n_kv;  // key/value loads per item
+  constexpr int nsteps = 1;       // key tiles per query tile and item
+  constexpr int kv_per_item = 2;  // key/value loads per item (one per tile)
 
   if (threadIdx.x == 0) {
     for (int b = 0; b < 2; ++b) {
@@ -143,7 +121,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
     for (int s = 0; s < kAttnKvStages; ++s) {
       mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], freq ? 1 : 2);  // time mode: both query tiles read every stage
+      mbar_init(&kv_empty[s], 1);  // each stage holds one tile's keys
     }
     mbar_init(drain, 2);
     *abort_flag = 0;
@@ -164,21 +142,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp < 4) {
-  if constexpr (!kFreq) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kAttnRegsLow) : "memory");
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
       int kvc = 0, local = 0, q_issued = 0;
       bool ok = true;
       for (int item = blockIdx.x; item < args.num_items && ok; item += gridDim.x, ++local) {
-        int bh, q0;
-        if (freq) {
-          bh = 4 * item;
-          q0 = 0;
-        } else {
-          bh = item / args.q_pairs;
-          q0 = (item - bh * args.q_pairs) * 256;
-        }
+        const int bh = 4 * item;  // first of the item's four sequences
         const int qb = local & 1;
         if (!mbar_wait(&q_empty[qb], ((uint32_t)(local >> 1) & 1) ^ 1, args.err, kErrWaitProducer, abort_flag)) {
           ok = false;
@@ -186,13 +156,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
         mbar_arrive_expect_tx(&q_full[qb], 2 * S::kTile);
         uint8_t* qbuf = smem + S::kQ + qb * 2 * S::kTile;
-        if (freq) {
-          tma_load_3d(qbuf, &map_q, &q_full[qb], 0, 0, bh);
-          tma_load_3d(qbuf + S::kTile, &map_q, &q_full[qb], 0, 0, bh + 2);
-        } else {
-          tma_load_3d(qbuf, &map_q, &q_full[qb], 0, q0, bh);
-          tma_load_3d(qbuf + S::kTile, &map_q, &q_full[qb], 0, q0 + 128, bh);
-        }
+        tma_load_3d(qbuf, &map_q, &q_full[qb], 0, 0, bh);
+        tma_load_3d(qbuf + S::kTile, &map_q, &q_full[qb], 0, 0, bh + 2);
         ++q_issued;
         for (int j = 0; j < kv_per_item; ++j) {
           const int st = kvc % kAttnKvStages;
@@ -203,10 +168,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           }
           uint8_t* kb = smem + S::kKV + st * 2 * S::kTile;
           mbar_arrive_expect_tx(&kv_full[st], 2 * S::kTile);
-          const int row = freq ? 0 : j * 128;
-          const int seq = freq ? bh + 2 * j : bh;
-          tma_load_3d(kb, &map_k, &kv_full[st], 0, row, seq);
-          tma_load_3d(kb + S::kTile, &map_v, &kv_full[st], 0, row, seq);
+          tma_load_3d(kb, &map_k, &kv_full[st], 0, 0, bh + 2 * j);
+          tma_load_3d(kb + S::kTile, &map_v, &kv_full[st], 0, 0, bh + 2 * j);
           ++kvc;
         }
       }
@@ -244,7 +207,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       };
       // S(j) = Q K(j)^T into this tile's S columns
       auto issue_s = [&](int j, uint64_t qd, int qb) {
-        const int idx = freq ? kvc + x : kvc + j;
+        const int idx = kvc + x;  // tile x's own key stage
         const int st = idx % kAttnKvStages;
         if (!wait(&kv_full[st], (uint32_t)(idx / kAttnKvStages) & 1)) return;
         tc_fence_after();
@@ -259,14 +222,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         if (!wait(&p_full[x], g & 1u)) return;
         if (j == 0 && local > 0 && !wait(&o_free[x], (uint32_t)(local - 1) & 1)) return;
         tc_fence_after();
-        const int idx = freq ? kvc + x : kvc + j;
+        const int idx = kvc + x;  // tile x's own key stage
         const int st = idx % kAttnKvStages;
         const uint64_t vd = v_desc0 + (uint64_t)(st * kStep);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)  // 16 keys per MMA: P columns kk*8.., V rows kk*16..
           mma_f16_ts(tO, tP + kk * 8, vd + kk * (2048 >> 4), idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
         mma_commit(&p_free[x]);
-        mma_commit(&kv_empty[st]);  // one of the stage's readers (two in time mode)
+        mma_commit(&kv_empty[st]);
       };
       for (int item = blockIdx.x; item < args.num_items && ok; item += gridDim.x, ++local) {
         const int qb = local & 1;
@@ -289,7 +252,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
   }
   } else {
-    if constexpr (!kFreq) asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kAttnRegsHigh) : "memory");
     // ------------------------------------------------------------------ softmax + epilogue (warps 4-11)
     const int x = (warp - 4) >> 2;  // query tile of this warpgroup
     const int quarter = warp & 3;
@@ -302,23 +264,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     uint32_t g = 0;  // steps of this tile so far, all items (s_full / p_free phases)
     // This thread's query row of an item: output token, false if the row lies outside its sequence.
     auto row_token = [&](int item, long* token) -> bool {
-      int seq, pos;
-      if (freq) {
-        seq = 4 * item + 2 * x + (r >> 6);
-        pos = r & 63;
-      } else {
-        const int bh = item / args.q_pairs;
-        seq = bh;
-        pos = (item - bh * args.q_pairs) * 256 + x * 128 + r;
-      }
+      const int seq = 4 * item + 2 * x + (r >> 6);
+      const int pos = r & 63;
       if (pos >= args.L || seq >= args.BH) return false;
-      const int grp = seq >> 3;
-      if (!freq) {  // grp = b*F + f, pos = t
-        const int b = grp / args.F, f = grp - b * args.F;
-        *token = (((long)b * args.T + pos) * args.F + f) * 8 + (seq & 7);
-      } else {  // grp = b*T + t, pos = f
-        *token = ((long)grp * args.F + pos) * 8 + (seq & 7);
-      }
+      const int grp = seq >> 3;  // grp = b*T + t, pos = f
+      *token = ((long)grp * args.F + pos) * 8 + (seq & 7);
       return true;
     };
     // The epilogue of an item (read O, release it, scale by gate / l, store) is deferred until the next
@@ -360,150 +310,60 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           break;
         }
         tc_fence_after();
-        if constexpr (freq) {
-          // a row's keys are the 64 columns of its own sequence (block quarter / 2 of the tile); the other
-          // block's P is zero, and only keys < L exist. One key tile per item: no rescaling.
-          const int blk = quarter >> 1;
-          float sf[64];
-          tmem_ld64(tS + blk * 64, sf);
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&s_free[x]);
-#pragma unroll
-          for (int i = 0; i < 64; ++i)
-            if (i >= args.L) sf[i] = -INFINITY;
-          float mx4[4] = {sf[0], sf[1], sf[2], sf[3]};
-#pragma unroll
-          for (int i = 4; i < 60; i += 8) {
-            mx4[0] = fmax3(mx4[0], sf[i], sf[i + 4]);
-            mx4[1] = fmax3(mx4[1], sf[i + 1], sf[i + 5]);
-            mx4[2] = fmax3(mx4[2], sf[i + 2], sf[i + 6]);
-            mx4[3] = fmax3(mx4[3], sf[i + 3], sf[i + 7]);
-          }
-          m_run = fmaxf(fmax3(mx4[0], mx4[1], sf[60]), fmax3(mx4[2], mx4[3], fmax3(sf[61], sf[62], sf[63]))) * kLog2e;
-          const float2 scale2 = make_float2(kLog2e, kLog2e);
-          const float2 shift2 = make_float2(-m_run, -m_run);
-          float2 l2 = make_float2(0.f, 0.f);
-          uint32_t pk0[16], pk1[16];
-#pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            const float2 xv = __ffma2_rn(make_float2(sf[i], sf[i + 1]), scale2, shift2);
-            const float2 pv = make_float2(ex2_approx(xv.x), ex2_approx(xv.y));
-            l2 = __fadd2_rn(l2, pv);
-            pk0[i >> 1] = OperandType<TIn>::pack2(pv.x, pv.y);
-            const float2 xw = __ffma2_rn(make_float2(sf[32 + i], sf[33 + i]), scale2, shift2);
-            const float2 pw = make_float2(ex2_approx(xw.x), ex2_approx(xw.y));
-            l2 = __fadd2_rn(l2, pw);
-            pk1[i >> 1] = OperandType<TIn>::pack2(pw.x, pw.y);
-          }
-          l_run = l2.x + l2.y;
-          // P and O are this tile's again once the previous item's O = P V has completed
-          if (g > 0 && !mbar_wait_warp(&p_free[x], (g - 1) & 1u, args.err, kErrWaitSoftmax, abort_flag)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          uint32_t z[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) z[i] = 0u;
-          tmem_st16(tP + blk * 32, pk0);
-          tmem_st16(tP + blk * 32 + 16, pk1);
-          tmem_st16(tP + (1 - blk) * 32, z);
-          tmem_st16(tP + (1 - blk) * 32 + 16, z);
-          tmem_wait_st();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&p_full[x]);
-          if (item != (int)blockIdx.x) finish(item - gridDim.x);  // its O = P V completed: p_free above
-          continue;
-        }
-        // the whole score row in registers (one TMEM read); the S columns are then free for the next S
-        float sc[128];
-        tmem_ld128(tS, sc);
+        // a row's keys are the 64 columns of its own sequence (block quarter / 2 of the tile); the other
+        // block's P is zero, and only keys < L exist. One key tile per item: no rescaling.
+        const int blk = quarter >> 1;
+        float sf[64];
+        tmem_ld64(tS + blk * 64, sf);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&s_free[x]);
-        // keys past the sequence's end -> -inf
-        const int key0 = j * 128;
-        const int kmax = min(128, args.L - key0);  // keys of this tile that exist
-        if (kmax < 128) {
 #pragma unroll
-          for (int i = 0; i < 128; ++i)
-            if (i >= kmax) sc[i] = -INFINITY;
-        }
-        float mx4[4] = {sc[0], sc[1], sc[2], sc[3]};
+        for (int i = 0; i < 64; ++i)
+          if (i >= args.L) sf[i] = -INFINITY;
+        float mx4[4] = {sf[0], sf[1], sf[2], sf[3]};
 #pragma unroll
-        for (int i = 4; i < 124; i += 8) {
-          mx4[0] = fmax3(mx4[0], sc[i], sc[i + 4]);
-          mx4[1] = fmax3(mx4[1], sc[i + 1], sc[i + 5]);
-          mx4[2] = fmax3(mx4[2], sc[i + 2], sc[i + 6]);
-          mx4[3] = fmax3(mx4[3], sc[i + 3], sc[i + 7]);
+        for (int i = 4; i < 60; i += 8) {
+          mx4[0] = fmax3(mx4[0], sf[i], sf[i + 4]);
+          mx4[1] = fmax3(mx4[1], sf[i + 1], sf[i + 5]);
+          mx4[2] = fmax3(mx4[2], sf[i + 2], sf[i + 6]);
+          mx4[3] = fmax3(mx4[3], sf[i + 3], sf[i + 7]);
         }
-        const float m_tile =
-            fmaxf(fmax3(mx4[0], mx4[1], sc[124]), fmax3(mx4[2], mx4[3], fmax3(sc[125], sc[126], sc[127]))) *
-            kLog2e;
-        bool rescale = false;
-        float alpha = 1.0f;
-        if (j == 0) {
-          m_run = m_tile;
-        } else {
-          const bool need = m_tile > m_run + kRescaleThreshold;
-          rescale = __any_sync(0xffffffffu, need);
-          if (need) {
-            alpha = ex2_approx(m_run - m_tile);
-            m_run = m_tile;
-          }
-        }
-        // P = 2^(s log2e - m_run) as 16-bit pairs, 32 keys at a time; the last pair of every four on the
-        // FMA pipe
+        m_run = fmaxf(fmax3(mx4[0], mx4[1], sf[60]), fmax3(mx4[2], mx4[3], fmax3(sf[61], sf[62], sf[63]))) * kLog2e;
         const float2 scale2 = make_float2(kLog2e, kLog2e);
         const float2 shift2 = make_float2(-m_run, -m_run);
         float2 l2 = make_float2(0.f, 0.f);
-        auto exp_chunk = [&](int c, uint32_t(&packed)[16]) {
+        uint32_t pk0[16], pk1[16];
 #pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            const int k = c * 32 + i;
-            const float2 xv = __ffma2_rn(make_float2(sc[k], sc[k + 1]), scale2, shift2);
-            const float2 pv = (i & 7) == 6 ? ex2_poly2(xv) : make_float2(ex2_approx(xv.x), ex2_approx(xv.y));
-            l2 = __fadd2_rn(l2, pv);
-            packed[i >> 1] = OperandType<TIn>::pack2(pv.x, pv.y);
-          }
-        };
-        {
-          uint32_t packed[16];
-          exp_chunk(0, packed);
-          // P and O are this tile's again once the previous O += P V has completed
-          if (g > 0 && !mbar_wait_warp(&p_free[x], (g - 1) & 1u, args.err, kErrWaitSoftmax, abort_flag)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          if (rescale) {  // O holds the steps < j; 16 columns at a time (register budget)
-#pragma unroll 1
-            for (int h = 0; h < 4; ++h) {
-              float o[16];
-              uint32_t u[16];
-              tmem_ld16(tO + h * 16, o);
-#pragma unroll
-              for (int i = 0; i < 16; ++i) u[i] = __float_as_uint(o[i] * alpha);
-              tmem_st16(tO + h * 16, u);
-            }
-          }
-          tmem_st16(tP, packed);
+        for (int i = 0; i < 32; i += 2) {
+          const float2 xv = __ffma2_rn(make_float2(sf[i], sf[i + 1]), scale2, shift2);
+          const float2 pv = make_float2(ex2_approx(xv.x), ex2_approx(xv.y));
+          l2 = __fadd2_rn(l2, pv);
+          pk0[i >> 1] = OperandType<TIn>::pack2(pv.x, pv.y);
+          const float2 xw = __ffma2_rn(make_float2(sf[32 + i], sf[33 + i]), scale2, shift2);
+          const float2 pw = make_float2(ex2_approx(xw.x), ex2_approx(xw.y));
+          l2 = __fadd2_rn(l2, pw);
+          pk1[i >> 1] = OperandType<TIn>::pack2(pw.x, pw.y);
         }
-#pragma unroll
-        for (int c = 1; c < 4; ++c) {
-          uint32_t packed[16];
-          exp_chunk(c, packed);
-          tmem_st16(tP + c * 16, packed);
+        l_run = l2.x + l2.y;
+        // P and O are this tile's again once the previous item's O = P V has completed
+        if (g > 0 && !mbar_wait_warp(&p_free[x], (g - 1) & 1u, args.err, kErrWaitSoftmax, abort_flag)) {
+          ok = false;
+          break;
         }
-        l_run = l_run * alpha + (l2.x + l2.y);
+        tc_fence_after();
+        uint32_t z[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) z[i] = 0u;
+        tmem_st16(tP + blk * 32, pk0);
+        tmem_st16(tP + blk * 32 + 16, pk1);
+        tmem_st16(tP + (1 - blk) * 32, z);
+        tmem_st16(tP + (1 - blk) * 32 + 16, z);
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[x]);
-        // step 0 waited (p_free) for the previous item's last O += P V and did not rescale O
-        if (j == 0 && item != (int)blockIdx.x) finish(item - gridDim.x);
+        if (item != (int)blockIdx.x) finish(item - gridDim.x);  // its O = P V completed: p_free above
       }
       if (!ok) {
         alive = false;

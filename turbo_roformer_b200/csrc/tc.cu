@@ -2,6 +2,7 @@
 #include <atomic>
 
 #include "attention.cuh"
+#include "attention_time.cuh"
 #include "gemm.cuh"
 #include "internal.h"
 #include "mlp.cuh"
@@ -59,35 +60,47 @@ cudaError_t launch_gemm_p(int epi, const CUtensorMap& ma, const CUtensorMap& mb,
   }
 }
 
-template <typename T, bool kFreq>
-cudaError_t launch_attention_m(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
-                               const AttnArgs& args, int num_sms, cudaStream_t st) {
-  auto kern = attention_kernel<T, kFreq>;
-  static std::atomic<unsigned long long> done{0};  // one per <T, kFreq> instantiation
+template <typename T>
+cudaError_t launch_attention_freq(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
+                                  const AttnArgs& args, int num_sms, cudaStream_t st) {
+  auto kern = attention_freq_kernel<T>;
+  static std::atomic<unsigned long long> done{0};  // one per <T> instantiation
   cudaError_t e = allow_smem(kern, AttnSmem::kBytes, done);
   if (e != cudaSuccess) return e;
-  if (!kFreq) {
-    // the time-mode kernel moves registers between its warpgroups (setmaxnreg): the split must fit in
-    // what the launch gives the block, or the softmax warps' increase would never be granted
-    static std::atomic<int> regs{0};
-    if (regs.load() == 0) {
-      cudaFuncAttributes fa;
-      if ((e = cudaFuncGetAttributes(&fa, kern)) != cudaSuccess) return e;
-      regs.store(fa.numRegs);
-    }
-    if (4 * 32 * kAttnRegsLow + 8 * 32 * kAttnRegsHigh > kAttnThreads * regs.load()) return cudaErrorInvalidConfiguration;
-  }
   if (args.num_items <= 0) return cudaSuccess;
   const int grid = args.num_items < num_sms ? args.num_items : num_sms;
   kern<<<grid, kAttnThreads, AttnSmem::kBytes, st>>>(mq, mk, mv, args);
   return cudaGetLastError();
 }
 
+// Time mode: three query tiles per CTA (attention_time.cuh). The kernel moves registers between its
+// warpgroups (setmaxnreg): the split must fit in what the launch gives the block, or the softmax warps'
+// increase would never be granted.
+template <typename T>
+cudaError_t launch_attention_time(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
+                                  const AttnArgs& args, int num_sms, cudaStream_t st) {
+  auto kern = attention_time_kernel<T>;
+  static std::atomic<unsigned long long> done{0};
+  cudaError_t e = allow_smem(kern, TaSmem::kBytes, done);
+  if (e != cudaSuccess) return e;
+  static std::atomic<int> regs{0};
+  if (regs.load() == 0) {
+    cudaFuncAttributes fa;
+    if ((e = cudaFuncGetAttributes(&fa, kern)) != cudaSuccess) return e;
+    regs.store(fa.numRegs);
+  }
+  if (4 * 32 * kTaRegsLow + 12 * 32 * kTaRegsHigh > kTaThreads * regs.load()) return cudaErrorInvalidConfiguration;
+  if (args.num_items <= 0) return cudaSuccess;
+  const int grid = args.num_items < num_sms ? args.num_items : num_sms;
+  kern<<<grid, kTaThreads, TaSmem::kBytes, st>>>(mq, mk, mv, args);
+  return cudaGetLastError();
+}
+
 template <typename T>
 cudaError_t launch_attention_t(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                                const AttnArgs& args, int num_sms, cudaStream_t st) {
-  return args.mode == 1 ? launch_attention_m<T, true>(mq, mk, mv, args, num_sms, st)
-                        : launch_attention_m<T, false>(mq, mk, mv, args, num_sms, st);
+  return args.mode == 1 ? launch_attention_freq<T>(mq, mk, mv, args, num_sms, st)
+                        : launch_attention_time<T>(mq, mk, mv, args, num_sms, st);
 }
 
 }  // namespace
