@@ -54,7 +54,7 @@ CONFIG1_SAMPLES = 749_700  # one 17 s chunk, T = 1701 frames
 # `ncu --set full` on `bench.py --batch 1` (the one-chunk captures summarised under profiles/); a batched
 # launch moves this per chunk. None = not captured.
 TRAFFIC_PER_CHUNK = {
-    "attention_t": (327.78e6 + 86.99e6),
+    "attention_t": (327.54e6 + 86.24e6),
     "attention_f": (327.21e6 + 78.00e6),
     "qkv_rope_gemm": (56.79e6 + 269.93e6),
     "gemm_out_res_norm": (216.26e6 + 104.90e6),
