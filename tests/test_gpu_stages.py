@@ -187,6 +187,28 @@ def test_attention(tiny_cuda, tiny_cfg, mode, B, T):
     assert snr_db(ref.reshape(N, 512).numpy(), O.float().cpu().numpy()) >= 50.0
 
 
+@pytest.mark.parametrize("T", [1, 63, 64, 65, 129, 256, 257, 384, 385, 640, 700])
+def test_attention_time_item_edges(tiny_cuda, tiny_cfg, T):
+    """Time mode around the kernel's item and step edges: items of three 128-row query tiles (a last item
+    with one, two or three tiles inside the sequence) and 64-key steps (a last step with 1..64 keys)."""
+    B, Fb = 1, tiny_cfg.n_bands
+    N = B * T * Fb
+    BH = N * 8 // T
+    g = torch.Generator().manual_seed(1000 + T)
+    Q = (torch.randn(BH, T, 64, generator=g) * 0.25).half()
+    K = (torch.randn(BH, T, 64, generator=g) * 0.25).half()
+    V = torch.randn(BH, T, 64, generator=g).half()
+    G = torch.rand(N, 8, generator=g)
+    o = attention_ref(Q, K, V, G, B, T, Fb, 0)
+    ref = from_sequences(o, B, T, Fb, 0).view(N, 8, 64) * G[:, :, None]
+    O = torch.full((N, 512), float("nan"), device="cuda", dtype=torch.float16)
+    Qd, Kd, Vd, Gd = Q.cuda(), K.cuda(), V.cuda(), G.cuda()
+    call(tiny_cuda, "trc_attention", 0, vp(Qd), vp(Kd), vp(Vd), vp(Gd), vp(O), B, T, stream(tiny_cuda))
+    got = O.float().cpu()
+    assert torch.isfinite(got).all()  # every output row written
+    assert snr_db(ref.reshape(N, 512).numpy(), got.numpy()) >= 50.0
+
+
 def test_attention_full_length(tiny_cuda, tiny_cfg):
     """Time attention over T = 1701 frames (14 key tiles, ragged last tile), a subset of sequences checked."""
     B, T, Fb = 1, 1701, tiny_cfg.n_bands
