@@ -109,7 +109,8 @@ int trc_ola(const float* d_chunks, int64_t chunk_out_len, const int64_t* h_start
 const char* trc_last_error(void);
 
 /* Replaces audio.to_stereo / downmix_stereo (turbo_roformer/audio.py:35-68) on the device:
- * d_out[o][i] = (float)(sum over k of h_gains[o * channels + k] * (double)d_in[k][i]), k ascending, fp64.
+ * d_out[o][i] = (float)(sum over k of h_gains[o * channels + k] * (double)d_in[k][i]), k ascending, fp64 with
+ * separately rounded products and sums.
  * d_in [channels][n] float32; h_gains: host (2 x channels) float64 row-major, copied into the launch;
  * 1 <= channels <= 16; d_out [2][n]. */
 int trc_remix(const float* d_in, int channels, int64_t n, const double* h_gains, float* d_out, void* stream);

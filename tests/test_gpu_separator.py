@@ -1,5 +1,6 @@
-"""Separator API on the CUDA backend (the reference's tests/test_separator.py cases that need no resampler or
-sound files), checked against the reference's own Separator output on the small model."""
+"""Separator API on the CUDA backend (the reference's tests/test_separator.py cases that need no sound
+files; the other-rate and surround cases are in test_gpu_resample.py), checked against the reference's own
+Separator output on the small model."""
 
 from __future__ import annotations
 

@@ -75,7 +75,13 @@ def to_stereo(x: np.ndarray) -> np.ndarray:
         return np.ascontiguousarray(x, dtype=np.float32)
     if x.shape[0] == 1:
         return np.ascontiguousarray(np.broadcast_to(x, (2, x.shape[1])), dtype=np.float32)
-    return (stereo_gains(x.shape[0]) @ x.astype(np.float64)).astype(np.float32)
+    # channel order, separately rounded products and sums in float64: the device fold (trc_remix) makes
+    # the same operations, so both give the same float32 result
+    g = stereo_gains(x.shape[0])
+    y = np.zeros((2, x.shape[1]))
+    for k in range(x.shape[0]):
+        y += g[:, k : k + 1] * x[k].astype(np.float64)
+    return y.astype(np.float32)
 
 
 def downmix_stereo(x: np.ndarray) -> np.ndarray:

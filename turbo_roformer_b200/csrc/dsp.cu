@@ -426,7 +426,8 @@ void launch_chunk_ola(const float* chunks, int64_t clen, const int64_t* d_starts
 
 // ------------------------------------------------------------------------------------------ remix / resample
 // Channel fold to stereo (audio.downmix_stereo / to_stereo, turbo_roformer/audio.py:35-68): one output
-// sample per thread and side, the channel sum in fp64 in channel order, rounded once to fp32.
+// sample per thread and side, the channel sum in fp64 in channel order with separately rounded products
+// and sums (the host fold's operations, so both agree bit for bit), rounded once to fp32.
 struct RemixGains {
   double g[2][kRemixMaxChannels];
 };
@@ -436,7 +437,7 @@ __global__ void __launch_bounds__(256) remix_kernel(const float* __restrict__ x,
   const int side = blockIdx.y;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     double acc = 0.0;
-    for (int k = 0; k < channels; ++k) acc = fma(gains.g[side][k], (double)__ldg(x + (size_t)k * n + i), acc);
+    for (int k = 0; k < channels; ++k) acc = __dadd_rn(acc, __dmul_rn(gains.g[side][k], (double)__ldg(x + (size_t)k * n + i)));
     y[(size_t)side * n + i] = (float)acc;
   }
 }
