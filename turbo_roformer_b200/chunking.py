@@ -149,7 +149,7 @@ def overlap_add_cuda(
     x: torch.Tensor,
     chunk: int,
     overlap: float,
-    batch: int = 4,
+    batch: int = 8,
     progress: Callable[[int, int], None] | None = None,
     check: bool = True,
 ) -> torch.Tensor:

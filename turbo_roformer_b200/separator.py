@@ -5,7 +5,8 @@ Same constructor shape, same ``separate`` / ``separate_file`` / ``n_chunks`` / `
 same chunking, short-clip padding, peak normalisation to 0.9, Hamming overlap-add and
 vocals = mix - instrumental. Differences: ``backend`` is ``"cuda"`` (``"auto"`` means the same), the
 precision names the tensor-core operand type (``"fp16"`` default, ``"bf16"``), ``device`` picks the GPU
-and ``batch`` is how many chunks share one forward call. Weights are never downloaded by this package:
+and ``batch`` is how many chunks share one forward call (8 by default: about 7 GB of work buffers, the
+batch the throughput figures use). Weights are never downloaded by this package:
 a registry name resolves to a checkpoint already present in ``model_dir``.
 """
 
@@ -77,7 +78,7 @@ class Separator:
         config: str | os.PathLike | None = None,
         progress: bool = True,
         device: int | None = None,
-        batch: int = 4,
+        batch: int = 8,
     ):
         self._check_args(precision, backend)
         t0 = time.perf_counter()
@@ -144,7 +145,7 @@ class Separator:
         backend: str = "cuda",
         threads: int | None = None,
         device: int | None = None,
-        batch: int = 4,
+        batch: int = 8,
     ) -> Separator:
         """Wrap an already constructed BS-RoFormer module (or its state dict) (separator.py:160-179)."""
         cls._check_args(precision, backend)
