@@ -468,13 +468,14 @@ def main() -> None:
         config = service_config(world, args.batch, chunk, T)
         metric = SERVICE_METRIC
 
+    # the clock sampler runs from the warm-up on, so its 200 ms samples cover the timed steps from the start
+    clocks = ClockSampler(local)
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
     barrier()
 
     # ---------------------------------------------------------------- timed region (device-resident input)
-    clocks = ClockSampler(local)
     launches0 = lib.trc_launch_count()
     torch.cuda.synchronize()
     barrier()
@@ -489,7 +490,16 @@ def main() -> None:
     ms = marks[0].elapsed_time(marks[-1])
     step_ms = [round(marks[k].elapsed_time(marks[k + 1]), 1) for k in range(args.steps)]
     launches = lib.trc_launch_count() - launches0
+    ms = max_over_ranks([ms], dev, world)[0]
+    # a timed region shorter than a second gets too few 200 ms clock samples: the same steps run on,
+    # untimed, for another 0.6 s (the same count on every rank), and the sampler stops after them
+    extra = int(np.ceil(600.0 / (ms / args.steps))) if ms < 1000.0 else 0
+    for _ in range(extra):
+        step()
+    torch.cuda.synchronize()
+    barrier()
     clk = clocks.stop()
+    clk["window"] = "warm-up and timed steps" + (f" and {extra} further untimed steps" if extra else "")
 
     # ---------------------------------------------------------------- per-section device time (one extra step)
     # Sections are bracketed by CUDA events inside the library; they run outside the timed region so the
@@ -509,7 +519,6 @@ def main() -> None:
         t = torch.tensor([float(launches)], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.SUM)
         launches = int(t[0])
-    ms = max_over_ranks([ms], dev, world)[0]
     value = args.steps * audio_per_step / (ms / 1e3)
 
     # ---------------------------------------------------------------- e2e through the public API
