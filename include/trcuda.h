@@ -42,8 +42,8 @@ extern "C" {
 typedef struct trc_handle trc_handle;
 
 /* Architecture of a single-stem stereo BS-RoFormer (turbo_roformer/model.py:181-245;
- * turbo_roformer/registry.py:49-69). Supported: dim 128, 256, 384 or 512 (256 runs the fused epilogue
- * kernels; the other widths run their residual branches as fp32 GEMMs followed by row norms, as the
+ * turbo_roformer/registry.py:49-69). Supported: dim a multiple of 64 in [128, 1024] (256 runs the fused
+ * epilogue kernels; the other widths run their residual branches as fp32 GEMMs followed by row norms, as the
  * reference drops its fused kernels for them, fast.py:121-122), 8 heads x 64, depth-1 time/freq
  * transformers, mask_estimator_depth 2, power-of-two n_fft in [256, 4096] with win_length == n_fft,
  * <= 64 bands. */

@@ -66,15 +66,16 @@ class ModelConfig:
         return self.stft_hop_length * (self.dim_t - 1)
 
     def validate_for_cuda(self) -> None:
-        """The CUDA backend supports what the reference's fused CPU path supports (fast.py:106-134), and
-        widths 128, 384 and 512 besides 256 (there the reference drops its fused kernels, fast.py:121-122;
-        here the 256-only fused epilogues are replaced by fp32 residual-branch GEMMs and row norms)."""
+        """The CUDA backend supports what the reference's fast CPU path supports (fast.py:106-134): besides
+        256, any width that is a multiple of 64 up to 1024 (there the reference drops its fused kernels,
+        fast.py:121-122; here the 256-only fused epilogues are replaced by fp32 residual-branch GEMMs and
+        row norms)."""
         if self.num_stems != 1 or self.audio_channels != 2:
             raise NotImplementedError("only single-stem stereo BS-RoFormer models are supported")
         if (self.heads, self.dim_head) != (8, 64):
             raise NotImplementedError(f"only heads=8, dim_head=64 is supported (got {self.heads}, {self.dim_head})")
-        if self.dim not in (128, 256, 384, 512):
-            raise NotImplementedError(f"dim must be 128, 256, 384 or 512 (got {self.dim})")
+        if self.dim % 64 or not 128 <= self.dim <= 1024:
+            raise NotImplementedError(f"dim must be a multiple of 64 in [128, 1024] (got {self.dim})")
         if self.time_transformer_depth != 1 or self.freq_transformer_depth != 1:
             raise NotImplementedError("only time/freq transformer depth 1 is supported")
         if self.mask_estimator_depth != 2:

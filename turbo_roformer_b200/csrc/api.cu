@@ -826,8 +826,8 @@ const char* trc_last_error(void) { return g_last_error.c_str(); }
 int trc_create(const trc_config* cfg, int device, trc_handle** out) {
   if (!cfg || !out) return fail(TRC_E_INVALID, "null argument");
   *out = nullptr;
-  if (cfg->dim != 128 && cfg->dim != 256 && cfg->dim != 384 && cfg->dim != 512)
-    return fail(TRC_E_INVALID, "dim must be 128, 256, 384 or 512");
+  if (cfg->dim % 64 || cfg->dim < 128 || cfg->dim > 1024)
+    return fail(TRC_E_INVALID, "dim must be a multiple of 64 in [128, 1024]");
   if (cfg->heads != 8 || cfg->dim_head != 64) return fail(TRC_E_INVALID, "only heads=8, dim_head=64 is supported");
   if (cfg->depth < 1) return fail(TRC_E_INVALID, "depth must be >= 1");
   const int n = cfg->n_fft;

@@ -240,52 +240,67 @@ __global__ void add_rmsnorm_kernel(float* __restrict__ X, const float* __restric
   }
 }
 
-// Rows of any width 128 * NV (models whose width is not 256): X (+)= Y, out = X / max(|X|, eps), one warp
-// per row, lane l holding float4s l, l + 32, ... of the row.
-template <typename TOut, int NV>
+// Rows of any width 64 * M (models whose width is not 256): X (+)= Y, out = X / max(|X|, eps), one warp
+// per row, lane l holding the float2s l, l + 32, ... of the row (every access a coalesced 256-byte row
+// segment per warp).
+template <typename TOut, int M>
 __global__ void add_rmsnorm_d_kernel(float* __restrict__ X, const float* __restrict__ Y, void* __restrict__ out,
                                      int out_f32, int64_t rows, float eps) {
-  constexpr int D = 128 * NV;
+  constexpr int D = 64 * M;
   const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
-  float4* xr = reinterpret_cast<float4*>(X + row * D);
-  float4 v[NV];
+  float2* xr = reinterpret_cast<float2*>(X + row * D);
+  float2 v[M];
   float ss = 0.f;
 #pragma unroll
-  for (int i = 0; i < NV; ++i) {
+  for (int i = 0; i < M; ++i) {
     v[i] = xr[i * 32 + lane];
     if (Y) {
-      const float4 y = reinterpret_cast<const float4*>(Y + row * D)[i * 32 + lane];
-      v[i].x += y.x; v[i].y += y.y; v[i].z += y.z; v[i].w += y.w;
+      const float2 y = reinterpret_cast<const float2*>(Y + row * D)[i * 32 + lane];
+      v[i].x += y.x;
+      v[i].y += y.y;
       xr[i * 32 + lane] = v[i];
     }
-    ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+    ss += v[i].x * v[i].x + v[i].y * v[i].y;
   }
 #pragma unroll
   for (int d = 16; d > 0; d >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, d);
   const float inv = 1.0f / fmaxf(sqrtf(ss), eps);
 #pragma unroll
-  for (int i = 0; i < NV; ++i) {
+  for (int i = 0; i < M; ++i) {
     if (out_f32)
-      reinterpret_cast<float4*>(static_cast<float*>(out) + row * D)[i * 32 + lane] =
-          make_float4(v[i].x * inv, v[i].y * inv, v[i].z * inv, v[i].w * inv);
+      reinterpret_cast<float2*>(static_cast<float*>(out) + row * D)[i * 32 + lane] = make_float2(v[i].x * inv, v[i].y * inv);
     else
-      reinterpret_cast<uint2*>(static_cast<TOut*>(out) + row * D)[i * 32 + lane] =
-          make_uint2(OperandType<TOut>::pack2(v[i].x * inv, v[i].y * inv),
-                     OperandType<TOut>::pack2(v[i].z * inv, v[i].w * inv));
+      reinterpret_cast<uint32_t*>(static_cast<TOut*>(out) + row * D)[i * 32 + lane] =
+          OperandType<TOut>::pack2(v[i].x * inv, v[i].y * inv);
   }
+}
+
+template <typename TOut, int M>
+void launch_norm_m(float* X, const float* Y, void* out, int out_f32, int64_t rows, float eps, cudaStream_t st) {
+  add_rmsnorm_d_kernel<TOut, M><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(X, Y, out, out_f32, rows, eps);
 }
 
 template <typename TOut>
 void launch_add_rmsnorm_d(float* X, const float* Y, void* out, int out_f32, int64_t rows, float eps, int dim,
                           cudaStream_t st) {
-  const unsigned blocks = (unsigned)((rows + 7) / 8);
-  switch (dim) {
-    case 128: add_rmsnorm_d_kernel<TOut, 1><<<blocks, 256, 0, st>>>(X, Y, out, out_f32, rows, eps); break;
-    case 384: add_rmsnorm_d_kernel<TOut, 3><<<blocks, 256, 0, st>>>(X, Y, out, out_f32, rows, eps); break;
-    case 512: add_rmsnorm_d_kernel<TOut, 4><<<blocks, 256, 0, st>>>(X, Y, out, out_f32, rows, eps); break;
-    default: add_rmsnorm_d_kernel<TOut, 2><<<blocks, 256, 0, st>>>(X, Y, out, out_f32, rows, eps); break;
+  switch (dim / 64) {  // dim is a multiple of 64 in [128, 1024] (checked by trc_create)
+    case 2: launch_norm_m<TOut, 2>(X, Y, out, out_f32, rows, eps, st); break;
+    case 3: launch_norm_m<TOut, 3>(X, Y, out, out_f32, rows, eps, st); break;
+    case 4: launch_norm_m<TOut, 4>(X, Y, out, out_f32, rows, eps, st); break;
+    case 5: launch_norm_m<TOut, 5>(X, Y, out, out_f32, rows, eps, st); break;
+    case 6: launch_norm_m<TOut, 6>(X, Y, out, out_f32, rows, eps, st); break;
+    case 7: launch_norm_m<TOut, 7>(X, Y, out, out_f32, rows, eps, st); break;
+    case 8: launch_norm_m<TOut, 8>(X, Y, out, out_f32, rows, eps, st); break;
+    case 9: launch_norm_m<TOut, 9>(X, Y, out, out_f32, rows, eps, st); break;
+    case 10: launch_norm_m<TOut, 10>(X, Y, out, out_f32, rows, eps, st); break;
+    case 11: launch_norm_m<TOut, 11>(X, Y, out, out_f32, rows, eps, st); break;
+    case 12: launch_norm_m<TOut, 12>(X, Y, out, out_f32, rows, eps, st); break;
+    case 13: launch_norm_m<TOut, 13>(X, Y, out, out_f32, rows, eps, st); break;
+    case 14: launch_norm_m<TOut, 14>(X, Y, out, out_f32, rows, eps, st); break;
+    case 15: launch_norm_m<TOut, 15>(X, Y, out, out_f32, rows, eps, st); break;
+    default: launch_norm_m<TOut, 16>(X, Y, out, out_f32, rows, eps, st); break;
   }
 }
 

@@ -21,7 +21,7 @@ void launch_istft(const float* xin, const float* mask, int B, int T, int n, int 
                   const float2* tw_inv, float* frames, float* out, cudaStream_t st);
 void launch_band_pack(const float* xin, int width, int rows, int nbands, const int* band_off, const int* pad_off,
                       int kp, void* a, int precision, cudaStream_t st);
-// rows of `dim` floats (128, 256, 384 or 512)
+// rows of `dim` floats (a multiple of 64 in [128, 1024])
 void launch_rownorm(const float* X, void* xn, int64_t rows, float eps, int precision, int dim, cudaStream_t st);
 void launch_add_rmsnorm(float* X, const float* Y, void* out, int out_f32, int64_t rows, float eps, int precision,
                         int dim, cudaStream_t st);
