@@ -154,6 +154,15 @@ def test_submit_queues_songs_and_matches_separate(sep):
     np.testing.assert_array_equal(sep.submit(songs[2]).result(), ref[2])  # the handle stays usable
 
 
+def test_submit_mono_and_surround_equal_separate(sep):
+    """Mono and 5.1 mixes queued with submit (folded on the GPU) equal separate() of the same mixes."""
+    mono = S.chunk_audio(SR * 2, seed=31)[0]
+    six = (np.random.default_rng(32).standard_normal((6, SR * 2)) * 0.2).astype(np.float32)
+    jobs = [sep.submit(mono), sep.submit(six)]
+    np.testing.assert_array_equal(jobs[0].result(), sep.separate(mono))
+    np.testing.assert_array_equal(jobs[1].result(), sep.separate(six))
+
+
 def test_service_load_overlap3(sep):
     """Service-style load (several songs queued, overlap 3) equals one-at-a-time separation."""
     songs = [S.chunk_audio(SR * 2 + 1000 * k, seed=60 + k) for k in range(4)]

@@ -220,7 +220,8 @@ class Separator:
         return self._submit_device(src.to(self.device, non_blocking=True), n0, overlap, progress, out, src)
 
     @torch.inference_mode()
-    def _submit_resampled(self, x: np.ndarray, sr: int, overlap: float, progress) -> "SeparationJob":
+    def _submit_resampled(self, x: np.ndarray, sr: int, overlap: float, progress,
+                          out: torch.Tensor | None = None) -> "SeparationJob":
         """Any channel count and sample rate: the channel fold and both rate conversions on the GPU
         (``resample.remix_device`` / ``resample_device``), the 44.1 kHz part as ``_submit_44k``.
         The reference does these on the host (separator.py:214-230, audio.py:35-82)."""
@@ -234,7 +235,8 @@ class Separator:
         n0 = xd.shape[1]
         xd = torch.nn.functional.pad(xd, (0, self._padded_length(n0) - n0)).contiguous()
         post = (lambda inst: resample_device(inst.contiguous(), SR, sr, length=n)) if sr != SR else None
-        out = torch.empty((2, n), dtype=torch.float32, pin_memory=True)
+        if out is None:
+            out = torch.empty((2, n), dtype=torch.float32, pin_memory=True)
         return self._submit_device(xd, n0, overlap, progress, out, src, post)
 
     def _submit_device(self, xd: torch.Tensor, n0: int, overlap: float, progress, out: torch.Tensor | None,
@@ -312,7 +314,8 @@ class Separator:
     def submit(self, mix, overlap: float = 2.0, out: torch.Tensor | None = None) -> "SeparationJob":
         """Queue one song on the GPU and return at once; ``job.result()`` waits for it.
 
-        Same input contract and result as ``separate`` for 44.1 kHz input (no resampling here). Several
+        Same input contract and result as ``separate`` for 44.1 kHz input (no resampling here; mono and
+        surround layouts are folded to stereo on the GPU). Several
         songs may be queued back to back: the host never synchronises between them, so the GPU stays busy
         while the host prepares the next song. A mix in pinned memory (a pinned CPU tensor) is copied by
         DMA straight from the caller's buffer; ``out`` may supply a pinned (2, n) float32 result buffer.
@@ -327,7 +330,10 @@ class Separator:
                 raise ValueError("empty input")
             x = mix.contiguous()
         else:
-            x = audio.to_stereo(audio.as_channels_first(mix, finite=False))
+            x = audio.as_channels_first(mix, finite=False)
+            if x.shape[0] != 2:
+                with self._lock:
+                    return self._submit_resampled(x, SR, float(overlap), None, out)
         with self._lock:
             return self._submit_44k(x, float(overlap), None, out)
 
