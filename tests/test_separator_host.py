@@ -172,3 +172,75 @@ def test_stream_logic_matches_whole_song_overlap_add(monkeypatch, overlap, batch
             assert st.samples_out == max(0, min(i, n) - C)
         parts.append(st.close())
         np.testing.assert_array_equal(np.concatenate(parts, axis=1), ref)
+
+
+class _FakeSoundfile:
+    """In-memory stand-in for the optional 'soundfile' package: read returns a stored (samples, channels)
+    array, write records what would have been encoded."""
+
+    def __init__(self, frames, sr):
+        self.frames, self.sr, self.written = frames, sr, {}
+
+    def read(self, path, dtype="float32", always_2d=True):
+        assert dtype == "float32" and always_2d
+        return self.frames.copy(), self.sr
+
+    def write(self, path, data, sr, subtype=None, format=None):
+        self.written[path] = (np.array(data), sr, subtype, format)
+
+
+@pytest.mark.parametrize("channels,sr", [(2, 44100), (1, 48000), (6, 44100)])
+def test_separate_file_writes_stems_and_reports(monkeypatch, tmp_path, channels, sr):
+    """separate_file (separator.py:234-283) on a stand-in decoder and model: the stems are the folded mix's
+    instrumental and mix - instrumental, written per format as <stem>_<name>.<fmt> with the reference's
+    encodings, and the result carries the reference's keys."""
+    import sys
+
+    rng = np.random.default_rng(channels)
+    frames = (0.3 * rng.standard_normal((5000, channels))).astype(np.float32)
+    sf = _FakeSoundfile(frames, sr)
+    monkeypatch.setitem(sys.modules, "soundfile", sf)
+    seen = {}
+
+    def fake_separate(self, mix, sr=44100, overlap=2.0, progress=None):
+        seen.update(mix=mix.copy(), sr=sr, overlap=overlap)
+        return (0.25 * mix).astype(np.float32)
+
+    monkeypatch.setattr(Separator, "separate", fake_separate)
+    sep = _bare(chunk=1000, hop=10)
+    sep.backend, sep.precision = "cuda", "fp16"
+    res = sep.separate_file(tmp_path / "song.flac", tmp_path / "out", formats=("wav", "flac"), overlap=3.0)
+
+    mix = audio.to_stereo(frames.T)
+    np.testing.assert_array_equal(seen["mix"], mix)
+    assert seen["sr"] == sr and seen["overlap"] == 3.0
+    inst = (0.25 * mix).astype(np.float32)
+    expect = {"instrumental": inst, "vocals": mix - inst}
+    assert set(res["files"]) == {"instrumental.wav", "vocals.wav", "instrumental.flac", "vocals.flac"}
+    for key, path in res["files"].items():
+        name, fmt = key.split(".")
+        assert path == str(tmp_path / "out" / f"song_{name}.{fmt}")
+        data, w_sr, subtype, container = sf.written[path]
+        np.testing.assert_array_equal(data, expect[name].T)
+        assert (w_sr, subtype, container) == (sr, audio.FORMATS[fmt], fmt.upper())
+    assert res["instrumental"] == res["files"]["instrumental.wav"] and res["vocals"] == res["files"]["vocals.wav"]
+    assert (tmp_path / "out").is_dir()
+    assert res["sample_rate"] == sr and res["duration_s"] == pytest.approx(5000 / sr)
+    assert res["n_chunks"] == sep.n_chunks(round(5000 * 44100 / sr), 3.0)
+    assert res["backend"] == "cuda" and res["precision"] == "fp16"
+    for k in ("read_s", "separate_s", "write_s"):
+        assert res[k] >= 0.0
+    assert res["wall_s"] == pytest.approx(res["read_s"] + res["separate_s"] + res["write_s"])
+    assert res["rtf"] == pytest.approx(res["wall_s"] / res["duration_s"])
+
+
+@pytest.mark.parametrize("formats", [("mp3",), ("wav", "ogg"), ()])
+def test_separate_file_rejects_formats_before_reading(monkeypatch, tmp_path, formats):
+    import sys
+
+    sf = _FakeSoundfile(np.zeros((10, 2), np.float32), 44100)
+    monkeypatch.setitem(sys.modules, "soundfile", sf)
+    monkeypatch.setattr(sf, "read", lambda *a, **k: pytest.fail("read before the formats were checked"))
+    with pytest.raises(ValueError):
+        _bare().separate_file(tmp_path / "x.wav", tmp_path, formats=formats)
+    assert not sf.written

@@ -381,44 +381,59 @@ class Separator:
         overlap: float = 2.0,
         progress: Callable[[int, int], None] | None = None,
     ) -> dict[str, Any]:
-        """Write ``<stem>_instrumental.<fmt>`` and ``<stem>_vocals.<fmt>``; returns paths and timings
-        (separator.py:234-283)."""
+        """Decode ``in_path``, separate it and write ``<stem>_instrumental.<fmt>`` and ``<stem>_vocals.<fmt>``
+        into ``out_dir`` for every format (separator.py:234-283).
+
+        Returns the first format's two paths (``instrumental``, ``vocals``), every path under ``files``
+        (keyed ``"<name>.<fmt>"``), the phase times ``read_s`` / ``separate_s`` / ``write_s`` / ``wall_s``,
+        ``rtf`` = wall_s / duration_s, ``sample_rate``, ``n_chunks`` (at 44.1 kHz), ``backend`` and
+        ``precision``. Unknown or missing formats raise ``ValueError`` before the file is read."""
+        formats = tuple(formats)
+        if not formats:
+            raise ValueError("at least one output format is needed")
         for fmt in formats:
             if fmt not in audio.output_formats():
                 raise ValueError(f"unsupported output format {fmt!r}")
-        t0 = time.perf_counter()
-        mix, sr = audio.load(in_path)
-        t1 = time.perf_counter()
-        stereo = audio.to_stereo(audio.as_channels_first(mix))
-        inst = self.separate(stereo, sr=sr, overlap=overlap, progress=progress)
-        vocals = stereo - inst
-        t2 = time.perf_counter()
-        out = Path(out_dir)
-        out.mkdir(parents=True, exist_ok=True)
-        stem = Path(in_path).stem
-        files: dict[str, str] = {}
-        for fmt in formats:
-            for name, data in (("instrumental", inst), ("vocals", vocals)):
-                p = out / f"{stem}_{name}.{fmt}"
-                audio.write(p, data, sr, fmt)
-                files[f"{name}.{fmt}"] = str(p)
-        t3 = time.perf_counter()
-        duration = stereo.shape[1] / sr
-        return dict(
-            instrumental=files[f"instrumental.{formats[0]}"],
-            vocals=files[f"vocals.{formats[0]}"],
-            files=files,
-            duration_s=duration,
-            sample_rate=sr,
-            n_chunks=self.n_chunks(round(stereo.shape[1] * SR / sr), overlap),
-            read_s=t1 - t0,
-            separate_s=t2 - t1,
-            write_s=t3 - t2,
-            wall_s=t3 - t0,
-            rtf=(t3 - t0) / duration,
-            backend=self.backend,
-            precision=self.precision,
-        )
+        clock = [time.perf_counter()]
+        decoded, sr = audio.load(in_path)
+        clock.append(time.perf_counter())
+        mix = audio.to_stereo(audio.as_channels_first(decoded))
+        inst = self.separate(mix, sr=sr, overlap=overlap, progress=progress)
+        stems = {"instrumental": inst, "vocals": mix - inst}
+        clock.append(time.perf_counter())
+        files = _write_stems(Path(out_dir), Path(in_path).stem, stems, sr, formats)
+        clock.append(time.perf_counter())
+        read_s, separate_s, write_s = (b - a for a, b in zip(clock, clock[1:]))
+        wall_s = clock[-1] - clock[0]
+        duration_s = mix.shape[1] / sr
+        first = formats[0]
+        return {
+            "instrumental": files[f"instrumental.{first}"],
+            "vocals": files[f"vocals.{first}"],
+            "files": files,
+            "duration_s": duration_s,
+            "sample_rate": sr,
+            "n_chunks": self.n_chunks(round(mix.shape[1] * SR / sr), overlap),  # the 44.1 kHz length run
+            "read_s": read_s,
+            "separate_s": separate_s,
+            "write_s": write_s,
+            "wall_s": wall_s,
+            "rtf": wall_s / duration_s,
+            "backend": self.backend,
+            "precision": self.precision,
+        }
+
+
+def _write_stems(out: Path, stem: str, stems: dict[str, np.ndarray], sr: int, formats: tuple[str, ...]) -> dict[str, str]:
+    """Encode each stem in each format as ``out/<stem>_<name>.<fmt>``; returns ``{"<name>.<fmt>": path}``."""
+    out.mkdir(parents=True, exist_ok=True)
+    files: dict[str, str] = {}
+    for fmt in formats:
+        for name, data in stems.items():
+            path = out / f"{stem}_{name}.{fmt}"
+            audio.write(path, data, sr, fmt)
+            files[f"{name}.{fmt}"] = str(path)
+    return files
 
 
 class _Song:
