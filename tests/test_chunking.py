@@ -47,13 +47,12 @@ def test_hamming_matches_numpy_and_golden(golden_tiny):
     assert hamming(1000).min() > 0.07
 
 
+# The overlap-add semantics of the reference's own tests, on the oracle (CPU) ...
 @pytest.mark.parametrize("n", [700, 1000, 4321, 10007])
 @pytest.mark.parametrize("overlap", [1.0, 1.5, 2.0, 3.0])
 def test_identity_model_reconstructs_input(n, overlap):
     x = torch.randn(2, n)
-    y = overlap_add(x, 1000, overlap, lambda c: c)
-    torch.testing.assert_close(y, x, rtol=0, atol=1e-5)
-    torch.testing.assert_close(y, O.overlap_add(x, 1000, overlap, lambda c: c), rtol=0, atol=0)
+    torch.testing.assert_close(O.overlap_add(x, 1000, overlap, lambda c: c), x, rtol=0, atol=1e-5)
 
 
 @pytest.mark.parametrize("overlap", [1.5, 2.0, 3.0])
@@ -61,18 +60,51 @@ def test_no_click_with_chunk_dependent_model(overlap):
     n, chunk = 100_000, 16000
     x = torch.ones(2, n)
     gains = iter([0.8, 1.2] * 100)
-    y = overlap_add(x, chunk, overlap, lambda c: c * next(gains)).numpy()
+    y = O.overlap_add(x, chunk, overlap, lambda c: c * next(gains)).numpy()
     assert y.min() >= 0.8 - 1e-6 and y.max() <= 1.2 + 1e-6
     assert np.abs(np.diff(y, axis=1)).max() < 0.25 * 0.4
-    hard = overlap_add(x, chunk, 1.0, lambda c: c * next(gains)).numpy()
+    hard = O.overlap_add(x, chunk, 1.0, lambda c: c * next(gains)).numpy()
     assert np.abs(np.diff(hard, axis=1)).max() > 0.39
 
 
-def test_progress_callback_counts():
+def test_overlap_add_has_no_host_path():
+    """The package's overlap_add sums on the GPU only: host tensors with a plain callable are refused."""
+    with pytest.raises(ValueError):
+        overlap_add(torch.randn(2, 5000), 1000, 2.0, lambda c: c)
+
+
+# ... and the package's device overlap-add against the oracle, bit for bit (same chunk outputs)
+@pytest.mark.gpu
+@pytest.mark.parametrize("n", [700, 1000, 4321, 10007])
+@pytest.mark.parametrize("overlap", [1.0, 1.5, 2.0, 3.0])
+def test_device_overlap_add_equals_oracle(cuda_device, n, overlap):
+    x = torch.randn(2, n, generator=torch.Generator().manual_seed(n))
+    y = overlap_add(x.to(cuda_device), 1000, overlap, lambda c: c)
+    assert y.is_cuda
+    torch.testing.assert_close(y.cpu(), O.overlap_add(x, 1000, overlap, lambda c: c), rtol=0, atol=0)
+    torch.testing.assert_close(y.cpu(), x, rtol=0, atol=1e-5)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("overlap", [1.0, 1.5, 3.0])
+def test_device_overlap_add_chunk_dependent_model_equals_oracle(cuda_device, overlap):
+    n, chunk = 100_000, 16000
+    x = torch.rand(2, n, generator=torch.Generator().manual_seed(3))
+    g1, g2 = iter([0.75, 1.25] * 100), iter([0.75, 1.25] * 100)  # exact products on either device
+    y = overlap_add(x.to(cuda_device), chunk, overlap, lambda c: c * next(g1))
+    ref = O.overlap_add(x, chunk, overlap, lambda c: c * next(g2))
+    torch.testing.assert_close(y.cpu(), ref, rtol=0, atol=0)
+
+
+@pytest.mark.gpu
+def test_device_overlap_add_progress_and_short_outputs(cuda_device):
     calls = []
-    overlap_add(torch.randn(2, 5000), 1000, 2.0, lambda c: c, progress=lambda k, n: calls.append((k, n)))
+    x = torch.randn(2, 5000, generator=torch.Generator().manual_seed(4))
+    run = lambda c: c[..., :900]  # noqa: E731  (a model that returns fewer samples than the chunk)
+    y = overlap_add(x.to(cuda_device), 1000, 2.0, run, progress=lambda k, n: calls.append((k, n)))
     n = len(chunk_starts(5000, 1000, 500))
     assert calls == [(k, n) for k in range(1, n + 1)]
+    torch.testing.assert_close(y.cpu(), O.overlap_add(x, 1000, 2.0, run), rtol=0, atol=0)
 
 
 def test_invalid_schedule_arguments():

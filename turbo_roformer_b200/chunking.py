@@ -2,8 +2,8 @@
 
 ``chunk_starts`` / ``step_for`` / ``hamming`` follow the reference's schedule exactly (regular steps of
 floor(chunk / overlap), tail chunk aligned to the end; symmetric Hamming window). ``overlap_add`` keeps the
-reference's signature for any ``run`` callable; ``overlap_add_cuda`` is the device path used by the CUDA
-backend: chunks are batched through one model call per batch and the weighted sum runs in libtrcuda's
+reference's signature for any ``run`` callable on CUDA tensors; ``overlap_add_cuda`` is the device path used
+by the CUDA backend: chunks are batched through one model call per batch. Both sum in libtrcuda's
 overlap-add kernel, which accumulates in start order with separately rounded multiplies and adds, so
 the result is bit-identical to the reference's loop for identical chunk outputs.
 """
@@ -77,27 +77,32 @@ def overlap_add(
     run: Callable[[torch.Tensor], torch.Tensor],
     progress: Callable[[int, int], None] | None = None,
 ) -> torch.Tensor:
-    """x (2, n) -> (2, n) with any ``run`` mapping (1, 2, C) -> (1, 2, L <= C) (same contract as the reference).
+    """x (2, n) -> (2, n): the reference's helper (chunking.py:36-61) with the weighted sum on the GPU.
 
-    When ``run`` is a CUDA model (has ``forward_device``) and ``x`` is on its device, this dispatches to
-    ``overlap_add_cuda``.
-    """
-    if hasattr(run, "forward_device") and x.is_cuda:
-        return overlap_add_cuda(run, x, chunk, overlap, progress=progress)
+    ``run`` maps (1, 2, C) -> (1, 2, L); the first min(C, L) samples are kept, L the same for every chunk.
+    A CUDA model (``CudaBSRoformer``: it has ``forward_device``) takes the batched device path and x may
+    then be on the host (the result comes back to x's device). Any other ``run`` is called once per chunk,
+    in start order, on slices of x, which must already be a CUDA tensor; its outputs are summed by
+    libtrcuda's overlap-add kernel (start order, separately rounded multiply and add: bit-identical to
+    the reference's loop for the same chunk outputs). There is no host-side overlap-add."""
+    if hasattr(run, "forward_device"):
+        xd = x.to(device=run.device, dtype=torch.float32).contiguous()
+        return overlap_add_cuda(run, xd, chunk, overlap, progress=progress).to(x.device)
+    if not x.is_cuda:
+        raise ValueError("overlap_add sums on the GPU: pass x as a CUDA tensor, or a CudaBSRoformer as run")
     n = x.shape[1]
     C = min(chunk, n)
     starts = chunk_starts(n, C, step_for(C, overlap))
-    w = torch.from_numpy(hamming(C)).to(x.device)
-    result = torch.zeros(2, n, dtype=torch.float32, device=x.device)
-    weight = torch.zeros(n, dtype=torch.float32, device=x.device)
+    ys = []
     for i, s in enumerate(starts):
         y = run(x[:, s : s + C].unsqueeze(0).contiguous())[0]
-        L = min(C, y.shape[-1])
-        result[:, s : s + L] += y[:, :L].float() * w[:L]
-        weight[s : s + L] += w[:L]
+        ys.append(y[:, : min(C, y.shape[-1])])
         if progress is not None:
             progress(i + 1, len(starts))
-    return result.div_(weight.clamp_(min=1e-10))
+    if len({tuple(y.shape) for y in ys}) != 1 or ys[0].shape[0] != 2:
+        raise ValueError("run must return (1, 2, L) with the same L for every chunk")
+    chunks = torch.stack([y.to(device=x.device, dtype=torch.float32) for y in ys])
+    return ola_device(chunks, starts, C, n)
 
 
 def ola_device(chunks: torch.Tensor, starts: list[int], chunk: int, n: int, out: torch.Tensor | None = None) -> torch.Tensor:
