@@ -25,20 +25,22 @@ def rmsnorm(x: torch.Tensor, gamma: torch.Tensor) -> torch.Tensor:
 
 
 def rotary_angles(freqs: torch.Tensor, seq_len: int) -> torch.Tensor:
-    """fp32 angles (seq, dim), each frequency repeated for its (even, odd) pair (model.py:46-50)."""
+    """fp32 angles (seq, dim / 2): position times each pair's frequency (model.py:46-50)."""
     pos = torch.arange(seq_len, dtype=torch.float32)
-    ang = torch.einsum("i,f->if", pos, freqs.float())
-    return torch.repeat_interleave(ang, 2, dim=-1)
+    return pos[:, None] * freqs.float()[None, :]
 
 
 def rotate(t: torch.Tensor, freqs: torch.Tensor) -> torch.Tensor:
-    """Interleaved-pair rotary embedding in fp32 (model.py:52-59)."""
+    """Rotary embedding in fp32 on interleaved pairs (model.py:52-59): the pair (a, b) = (t[2i], t[2i+1])
+    at position p becomes (a cos - b sin, b cos + a sin) with angle p * freqs[i]."""
     ang = rotary_angles(freqs, t.shape[-2])
+    c, s = ang.cos(), ang.sin()
     tf = t.float()
-    x = tf.unflatten(-1, (-1, 2))
-    x1, x2 = x.unbind(-1)
-    rot_half = torch.stack((-x2, x1), dim=-1).flatten(-2)
-    return (tf * ang.cos() + rot_half * ang.sin()).to(t.dtype)
+    a, b = tf[..., 0::2], tf[..., 1::2]
+    out = torch.empty_like(tf)
+    out[..., 0::2] = a * c - b * s
+    out[..., 1::2] = b * c + a * s
+    return out.to(t.dtype)
 
 
 def attention(x: torch.Tensor, sd: dict, p: str, heads: int, dim_head: int) -> torch.Tensor:
@@ -52,8 +54,8 @@ def attention(x: torch.Tensor, sd: dict, p: str, heads: int, dim_head: int) -> t
     k = rotate(k, freqs)
     out = F.scaled_dot_product_attention(q, k, v)  # scale dim_head ** -0.5 (model.py:107)
     gates = F.linear(x, sd[p + "to_gates.weight"], sd[p + "to_gates.bias"])
-    out = out * gates.permute(0, 2, 1).unsqueeze(-1).sigmoid()
-    out = out.permute(0, 2, 1, 3).reshape(b, n, heads * dim_head)
+    out = out * torch.sigmoid(gates).transpose(1, 2)[..., None]  # one gate per (head, position)
+    out = out.transpose(1, 2).reshape(b, n, heads * dim_head)
     return F.linear(out, sd[p + "to_out.0.weight"])
 
 
@@ -89,9 +91,10 @@ def stft(audio: torch.Tensor, cfg) -> tuple[torch.Tensor, torch.Tensor]:
             return_complex=True,
         )
     )
-    _, nf, nt, _ = spec.shape
-    spec = spec.view(b, s, nf, nt, 2).permute(0, 2, 1, 3, 4).reshape(b, nf * s, nt, 2)
-    xin = spec.permute(0, 2, 1, 3).reshape(b, nt, nf * s * 2)
+    nf, nt = spec.shape[1], spec.shape[2]
+    # (b s) f t c -> b (f s) t c: the two channels of a frequency bin become neighbouring rows
+    spec = spec.reshape(b, s, nf, nt, 2).transpose(1, 2).reshape(b, nf * s, nt, 2)
+    xin = spec.transpose(1, 2).reshape(b, nt, nf * s * 2)
     return spec, xin
 
 
