@@ -244,3 +244,28 @@ def test_separate_file_rejects_formats_before_reading(monkeypatch, tmp_path, for
     with pytest.raises(ValueError):
         _bare().separate_file(tmp_path / "x.wav", tmp_path, formats=formats)
     assert not sf.written
+
+
+def test_training_config_hop_and_frames_defaults():
+    """The reference's config defaults (separator.py:125-126): hop 512, dim_t from inference, then audio,
+    then 801; a zero or missing dim_t falls through to the next section."""
+    from turbo_roformer_b200.separator import _hop_and_frames
+
+    assert _hop_and_frames({"model": {}}) == (512, 801)
+    assert _hop_and_frames({"model": {"stft_hop_length": 441}, "audio": {"dim_t": 1101}}) == (441, 1101)
+    assert _hop_and_frames({"model": {}, "inference": {"dim_t": 1700}, "audio": {"dim_t": 3}}) == (512, 1700)
+    assert _hop_and_frames({"model": {}, "inference": {"dim_t": 0}, "audio": {"dim_t": 5}}) == (512, 5)
+    assert _hop_and_frames({"model": {}, "inference": None}) == (512, 801)
+
+
+def test_model_resolution_errors(tmp_path):
+    """No downloads: a registry name without its checkpoint in model_dir, an unknown name, and a custom
+    checkpoint without its config each fail before any device work."""
+    with pytest.raises(FileNotFoundError):
+        Separator._resolve("resurrection", tmp_path, None)
+    with pytest.raises(KeyError):
+        Separator._resolve("no-such-model", tmp_path, None)
+    ckpt = tmp_path / "custom.ckpt"
+    ckpt.write_bytes(b"")
+    with pytest.raises(ValueError):
+        Separator._resolve(str(ckpt), None, None)

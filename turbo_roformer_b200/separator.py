@@ -60,6 +60,16 @@ def load_state_dict(path: str | os.PathLike) -> dict:
     return {k: v.float() for k, v in sd.items()}
 
 
+def _hop_and_frames(cfg: dict) -> tuple[int, int]:
+    """STFT hop and frames per chunk of a training config (separator.py:125-126): the hop is
+    ``model.stft_hop_length`` (512 when absent); ``dim_t`` is the first one set of the ``inference`` and
+    ``audio`` sections (801 when neither sets it)."""
+    hop = cfg["model"].get("stft_hop_length", 512)
+    sections = (cfg.get("inference") or {}, cfg.get("audio") or {})
+    dim_t = next((sec["dim_t"] for sec in sections if sec.get("dim_t")), 801)
+    return int(hop), int(dim_t)
+
+
 class Separator:
     """Vocal/instrumental separation with a BS-RoFormer model on a B200.
 
@@ -118,10 +128,7 @@ class Separator:
         import yaml
 
         with open(config, encoding="utf-8") as f:
-            cfg = yaml.safe_load(f)
-        mcfg = cfg["model"]
-        hop = int(mcfg.get("stft_hop_length", 512))
-        dim_t = int(cfg.get("inference", {}).get("dim_t") or cfg.get("audio", {}).get("dim_t") or 801)
+            hop, dim_t = _hop_and_frames(yaml.safe_load(f))
         return load_state_dict(p), hop, dim_t, p.name
 
     def _configure(self, sd, hop, dim_t, precision, device, batch) -> None:
