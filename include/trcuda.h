@@ -11,6 +11,12 @@
  * Separator serialises calls with a lock, turbo_roformer/separator.py:101,226); handles on different
  * devices may be driven from different host threads.
  *
+ * Devices: a function that takes a handle makes the handle's device current on the calling thread
+ * (cudaSetDevice) and leaves it current on return; the caller's stream must belong to that device.
+ * Functions without a handle (trc_ola, trc_ola_noalloc, trc_remix, trc_resample) run on the calling
+ * thread's current device. Restoring a previous device is left to the caller, because doing so from the
+ * library would create a CUDA context on a device the process may never have used.
+ *
  * The reference's drop-in surface for this path is the torch op library
  *   TORCH_LIBRARY(turbo_roformer, m)          (src/turbo_roformer/csrc/kernels.cpp:644-652)
  * driven by FastBSRoformer.forward            (src/turbo_roformer/fast.py:363-394)

@@ -1179,7 +1179,10 @@ static int hamming_cached(int64_t chunk, const float** out) {
   }
   float* d = nullptr;
   TRC_CUDA(cudaMalloc(&d, sizeof(float) * chunk));
-  TRC_CUDA(cudaMemcpy(d, w.data(), sizeof(float) * chunk, cudaMemcpyHostToDevice));
+  if (cudaError_t e = cudaMemcpy(d, w.data(), sizeof(float) * chunk, cudaMemcpyHostToDevice); e != cudaSuccess) {
+    cudaFree(d);  // not cached: the next call retries
+    return fail(TRC_E_CUDA, "Hamming window upload failed: %s", cudaGetErrorString(e));
+  }
   cache[{dev, chunk}] = d;
   *out = d;
   return TRC_OK;
@@ -1200,7 +1203,11 @@ int trc_ola(const float* d_chunks, int64_t chunk_out_len, const int64_t* h_start
   // the starts are a few hundred bytes: a pageable copy is staged at once and never waits on the stream
   int64_t* d_s = nullptr;
   TRC_CUDA(cudaMallocAsync(&d_s, sizeof(int64_t) * n_chunks, st));
-  TRC_CUDA(cudaMemcpyAsync(d_s, h_starts, sizeof(int64_t) * n_chunks, cudaMemcpyHostToDevice, st));
+  if (cudaError_t e = cudaMemcpyAsync(d_s, h_starts, sizeof(int64_t) * n_chunks, cudaMemcpyHostToDevice, st);
+      e != cudaSuccess) {
+    cudaFreeAsync(d_s, st);
+    return fail(TRC_E_CUDA, "chunk starts upload failed: %s", cudaGetErrorString(e));
+  }
   trc::launch_chunk_ola(d_chunks, chunk_out_len, d_s, n_chunks, d_w, n, d_result, st);
   g_launches += 1;
   cudaError_t e = cudaGetLastError();
